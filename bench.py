@@ -1,0 +1,410 @@
+"""Benchmark of the dequant-GEMM hot path on B200.
+
+Workload: the sharded 28672x8192 int4 symmetric g128 layer (W ~ N(0, 0.015),
+x ~ N(0, 1), seeded synthetic data; weight-quantizer_b200/workloads.py), at
+batch 4096 by default. One step = the layer applied to one batch: each rank
+runs the dequant-GEMM on its row shard, and for N > 1 the shards are
+all-gathered over NVLink (NCCL) and permuted into y [B, M] on every rank.
+
+Metric: GFLOP/s = 2*B*M*K / t (the reference's convention,
+src/ptqkit/measure.py:167, dequantization not counted), whole job, t = max over
+ranks of the CUDA-event time of K steps. Also reported: the same layer at the
+decode batches 1, 32 and 256 (weight-stream GB/s and GFLOP/s), the end-to-end
+number through the public API with host buffers, the dominant kernel's
+roofline, and the reference CPU kernel timed on this host.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch with torchrun (one process per GPU).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from typing import Any
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+M_ROWS, K_COLS, GROUP = 28672, 8192, 128
+WORKLOAD = "sharded_28672x8192_int4_g128"
+METRIC = "dequant-GEMM weight-stream GB/s & GFLOP/s vs B200 roofline, batch 1–4096"
+
+
+def _peaks() -> dict[str, Any]:
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen[str] | None = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict[str, Any]:
+        self.out.flush()
+        self.out.seek(0)
+        rows = [ln.split(",") for ln in self.out.read().strip().splitlines() if ln.strip()]
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for name, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def reference_arm(args: argparse.Namespace) -> None:
+    """The reference's own CPU kernel on this host's cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+
+    wl = importlib.import_module("weight-quantizer_b200.workloads")
+    kern = oracle.reference_kernels()
+    kind = "reference" if kern is not None else "port"
+    layer = wl.sharded_28672x8192(batches=(args.batch,))[0]
+    r = oracle.quantize_stored(layer.weight.numpy(), 4, True, GROUP)
+    sample = min(args.cpu_sample_rows, args.batch)
+    x = np.ascontiguousarray(layer.x[args.batch][:sample].numpy())
+    threads = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+
+    def call() -> None:
+        if kern is not None:
+            kern.dequant_gemm(x, r["q"], r["scales"], r["zeros"], None, GROUP, 4, threads)
+        else:
+            oracle.dequant_gemm(x, r["q"], r["scales"], r["zeros"], None, GROUP, 4, threads)
+
+    for _ in range(args.warmup):
+        call()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    t = sum(times) / len(times)
+    gflops = 2.0 * sample * M_ROWS * K_COLS / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gflops, 3), "unit": "GFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_COLS, "batch": args.batch, "bits": 4,
+                   "group_size": GROUP, "symmetric": True},
+        "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": threads, "kind": kind,
+                         "sample": f"{sample} of the {args.batch} batch rows per step, full layer, "
+                                   f"{'oracle/_ref (ptqkit _kernels.dequant_gemm)' if kern else 'C oracle'}"},
+        "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample(q: Any, scales: Any, zeros: Any, x: Any, seconds: float) -> dict[str, Any]:
+    import numpy as np
+
+    import oracle
+
+    kern = oracle.reference_kernels()
+    threads = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    x = np.ascontiguousarray(x)
+
+    def call() -> None:
+        if kern is not None:
+            kern.dequant_gemm(x, q, scales, zeros, None, GROUP, 4, threads)
+        else:
+            oracle.dequant_gemm(x, q, scales, zeros, None, GROUP, 4, threads)
+
+    call()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(2.0 * x.shape[0] * M_ROWS * K_COLS / t / 1e9, 3), "unit": "GFLOP/s",
+            "cores": threads, "kind": "reference" if kern is not None else "port",
+            "sample": f"batch {x.shape[0]} x full {M_ROWS}x{K_COLS} layer, median of {len(times)} calls "
+                      f"({'ptqkit _kernels.dequant_gemm built in oracle/_ref' if kern else 'C oracle'})"}
+
+
+def ours(args: argparse.Namespace) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    wq = importlib.import_module("weight-quantizer_b200")
+    wl = importlib.import_module("weight-quantizer_b200.workloads")
+    sharded = importlib.import_module("weight-quantizer_b200.sharded")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = _peaks()
+    batches = sorted(set([args.batch] + [b for b in args.sweep if b != args.batch]))
+    layer = wl.sharded_28672x8192(batches=tuple(b for b in batches if b in (1, 32, 256, 4096)))[0]
+    for b in batches:
+        if b not in layer.x:
+            layer.x[b] = torch.randn(b, K_COLS, generator=torch.Generator().manual_seed(b))
+    mp, ranges = sharded.shard_rows(M_ROWS, world)
+    r0, r1 = ranges[rank]
+    qw_rows = wq.quantize_weight(layer.weight[r0:r1].to(dev), layer.config)
+    full_qw = wq.QuantizedWeight(
+        codes=qw_rows.codes, scales=qw_rows.scales, zeros=qw_rows.zeros, bits=4, group_size=GROUP,
+        in_features=K_COLS, out_features=r1 - r0, symmetric=True, packed=True, granularity="group")
+    shard = sharded.shard_weight(full_qw, 0, 1) if (r1 - r0) == mp else None
+    if shard is None:
+        pad = mp - (r1 - r0)
+        shard = wq.QuantizedWeight(
+            codes=torch.cat((full_qw.codes, torch.zeros(pad, full_qw.codes.shape[1], dtype=torch.uint8, device=dev))),
+            scales=torch.cat((full_qw.scales, torch.ones(pad, full_qw.scales.shape[1], device=dev))),
+            zeros=torch.cat((full_qw.zeros, torch.zeros(pad, full_qw.zeros.shape[1], device=dev))),
+            bits=4, group_size=GROUP, in_features=K_COLS, out_features=mp, symmetric=True, packed=True,
+            granularity="group")
+    lin = sharded.RowParallelDequantLinear(shard, M_ROWS, rank, world)
+    weight_bytes_job = (M_ROWS * (K_COLS // 2)) + 2 * 4 * M_ROWS * (K_COLS // GROUP)
+    launches_per_step = 1 + (1 if world > 1 else 0)
+
+    stream = torch.cuda.current_stream(dev)
+    B = args.batch
+    x = layer.x[B].to(dev)
+
+    # ---- main line: K steps of the whole layer at batch B ------------------
+    for _ in range(args.warmup):
+        lin.forward(x)
+    torch.cuda.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            lin.forward(x)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    t_step = max_over_ranks(start.elapsed_time(end) / args.steps / 1e3)
+    flops = 2.0 * B * M_ROWS * K_COLS
+    value = flops / t_step / 1e9
+    clock = clocks.summary()
+
+    # ---- dominant kernel alone (local GEMM), for the roofline --------------
+    local_out = torch.empty((B, mp), dtype=torch.float32, device=dev)
+    kt = []
+    for i in range(args.warmup + args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        lin.forward_local(x, out=local_out)
+        e1.record(stream)
+        if i >= args.warmup:
+            kt.append((e0, e1))
+    torch.cuda.synchronize()
+    t_kernel = sum(a.elapsed_time(b) for a, b in kt) / len(kt) / 1e3
+    kernel_flops = 2.0 * B * mp * K_COLS
+    achieved_tflops = kernel_flops / t_kernel / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved_tflops, 3), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                "kernel": "dequant-GEMM (batch %d, %d rows per GPU)" % (B, mp),
+                "kernel_ms": round(t_kernel * 1e3, 4), "peak_source": peaks["source"]}
+
+    # ---- sweep: decode batches, L2 flushed between iterations --------------
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    sweep = []
+    for b in args.sweep:
+        if b == B:
+            continue
+        xb = layer.x[b].to(dev)
+        for _ in range(args.warmup):
+            lin.forward(xb)
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            e0.record(stream)
+            lin.forward(xb)
+            e1.record(stream)
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        t = max_over_ranks(statistics.median(a.elapsed_time(c) for a, c in ts) / 1e3)
+        kt2 = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            lin.forward_local(xb, out=local_out[:b])
+            e1.record(stream)
+            kt2.append((e0, e1))
+        torch.cuda.synchronize()
+        tk = statistics.median(a.elapsed_time(c) for a, c in kt2) / 1e3
+        shard_bytes = mp * (K_COLS // 2) + 2 * 4 * mp * (K_COLS // GROUP) + 4 * b * K_COLS + 4 * b * mp
+        sweep.append({
+            "batch": b, "ms": round(t * 1e3, 4), "gflops": round(2.0 * b * M_ROWS * K_COLS / t / 1e9, 1),
+            "weight_gbs": round(weight_bytes_job / t / 1e9, 1),
+            "kernel_ms": round(tk * 1e3, 4),
+            "kernel_hbm_gbs": round(shard_bytes / tk / 1e9, 1),
+            "kernel_hbm_frac": round(shard_bytes / tk / 1e9 / peaks["hbm_gbs"], 4),
+        })
+
+    # ---- end to end through the public API with pinned host buffers --------
+    e2e = None
+    if not args.no_e2e:
+        x_h = layer.x[B].pin_memory()
+        rows_per_rank = (B + world - 1) // world
+        b0, b1 = min(rank * rows_per_rank, B), min((rank + 1) * rows_per_rank, B)
+        y_h = torch.empty((b1 - b0, M_ROWS), dtype=torch.float32).pin_memory()
+        x_d = torch.empty_like(x)
+
+        def e2e_step() -> None:
+            x_d.copy_(x_h, non_blocking=True)
+            y = lin.forward(x_d)
+            y_h.copy_(y[b0:b1], non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t_e2e = max_over_ranks(s0.elapsed_time(s1) / args.steps / 1e3)
+        e2e = {"value": round(flops / t_e2e / 1e9, 1), "unit": "GFLOP/s",
+               "h2d_bytes_per_step": int(world * B * K_COLS * 4), "d2h_bytes_per_step": int(B * M_ROWS * 4),
+               "ms_per_step": round(t_e2e * 1e3, 3),
+               "path": "pinned x -> device, RowParallelDequantLinear.forward (dequant_gemm kernel"
+                       + (" + NCCL all-gather + permute" if world > 1 else "") + "), y rows -> pinned host"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = min(args.cpu_sample_rows, B)
+        cpu = cpu_baseline_sample(full_qw.codes.cpu().numpy(), full_qw.scales.cpu().numpy(),
+                                  full_qw.zeros.cpu().numpy(), layer.x[B][:sample].numpy(), args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded: W ~ N(0, 0.015), x ~ N(0, 1))",
+            "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_COLS, "batch": B, "bits": 4,
+                       "group_size": GROUP, "symmetric": True,
+                       "parallelism": f"row-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "l2": "working set larger than L2 (x 134 MB, y 470 MB, weights 132 MB at batch 4096); "
+                             "sweep lines flush L2 (256 MB write) between iterations"},
+            "weight_gbs": round(weight_bytes_job / t_step / 1e9, 1),
+            "clocks": {"sm_mhz": clock["sm_mhz"], "sm_max_mhz": clock["sm_max_mhz"], "reasons": clock["reasons"]},
+            "roofline": roofline,
+            "sweep": sweep,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps * launches_per_step,
+        }
+        print(json.dumps(line), flush=True)
+    del np
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=4096)
+    ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=[1, 32, 256])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-rows", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,163 @@
+/*
+ * wq_b200 — C ABI of the B200 (sm_100a) dequant-GEMM and RTN quantize+pack path.
+ *
+ * Drop-in replacement for the native kernel of ptqkit (cvs0/weight-quantizer),
+ * the pybind11 module `ptqkit._kernels` built from src/ptqkit/csrc/dequant_gemm.cpp,
+ * plus device versions of its RTN producer (src/ptqkit/quant.py) and int4 packing
+ * (src/ptqkit/pack.py). Storage layouts are ptqkit's, byte for byte:
+ *
+ *   x        fp32  [B, K]                      row-major activations
+ *   q        uint8 [M, K]          (bits 8)    one code per byte
+ *            uint8 [M, (K+1)/2]    (bits 4)    code 2j in the low nibble of byte j,
+ *                                              code 2j+1 in the high nibble; odd K
+ *                                              pads a zero nibble that is never read
+ *   scales   fp32  [scale_rows, groups]        scale_rows in {1, M}, groups = ceil(K/G)
+ *   zeros    fp32  [scale_rows, groups]
+ *   channel  fp32  [K] or absent               AWQ channel scale (stored 1/s)
+ *   y        fp32  [B, M]
+ *
+ *   y[b, m] = sum_k scale[m, g] * (q[m, k] - zero[m, g]) * channel[k] * x[b, k],  g = k / G
+ *
+ * Conventions
+ *   - All data pointers are DEVICE pointers of the current CUDA device. They are
+ *     borrowed, never freed. Shapes are element counts.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Work is enqueued on it; no entry point synchronizes the host.
+ *   - Every entry point returns 0 (WQ_OK) or a WQ_E_* status; wq_status_string()
+ *     gives the message. Argument errors are detected on the host before any
+ *     launch and use the reference's own messages where it has one.
+ *   - Results are deterministic: the same inputs and shapes give the same bits
+ *     on every call (no atomics in any reduction).
+ */
+#ifndef WQ_B200_H
+#define WQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WQ_API __attribute__((visibility("default")))
+#else
+#define WQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum wq_status {
+    WQ_OK = 0,
+    WQ_E_X_SHAPE = 1,        /* "x must have shape [B, K]" (dequant_gemm.cpp:235-237) */
+    WQ_E_RANK = 2,           /* "q, scales, and zeros must be rank 2" (:238-240) */
+    WQ_E_BITS = 3,           /* "bits must be 4 or 8" (:241-243) */
+    WQ_E_GROUP_SIZE = 4,     /* "group_size must be positive" (:244-246) */
+    WQ_E_NEG_DIM = 5,        /* "negative dimension" (:252-254) */
+    WQ_E_PACKED_COLS = 6,    /* "packed code row length does not match K" (:255-258) */
+    WQ_E_ZEROS_SHAPE = 7,    /* "zeros shape must match scales" (:259-261) */
+    WQ_E_SCALE_ROWS = 8,     /* "scale rows must be 1 or M" (:262-264) */
+    WQ_E_SCALE_GROUPS = 9,   /* "scale groups must equal ceil(K / group_size)" (:265-268) */
+    WQ_E_CHANNEL_SHAPE = 10, /* "channel_scale must have shape [K]" (:271-276) */
+    WQ_E_NULL = 11,          /* a required pointer is NULL */
+    WQ_E_WORKSPACE = 12,     /* workspace smaller than the *_workspace_bytes() query */
+    WQ_E_TOO_LARGE = 13,     /* a dimension is beyond what the kernels index */
+    WQ_E_CUDA = 14,          /* a CUDA call failed; wq_last_cuda_error() has the text */
+    WQ_E_NOT_FINITE = 15,    /* "weight must be finite" (quant.py:240-241) */
+    WQ_E_PRE_SCALE_LEN = 16, /* "pre_scale must have one entry per input channel" (quant.py:245-246) */
+    WQ_E_PRE_SCALE_VAL = 17, /* "pre_scale must be finite and positive" (quant.py:247-248) */
+    WQ_E_INT4_RANGE = 18,    /* "int4 codes must lie in [0, 15]" (pack.py:22-26) */
+    WQ_E_GROUP_MODE = 19,    /* "group_size must be None, 0, or positive" (quant.py:75-76) */
+    WQ_E_LD = 20             /* output row stride smaller than the row length */
+};
+
+/* Message for a status code (static storage; never NULL). */
+WQ_API const char* wq_status_string(int status);
+/* Text of the last CUDA error seen by this library on the calling thread. */
+WQ_API const char* wq_last_cuda_error(void);
+
+/* Build/device facts, the counterpart of `_kernels.kernel_info()`
+ * (dequant_gemm.cpp:302-315, which reports {"avx2", "openmp"}). */
+typedef struct wq_kernel_info_t {
+    int abi_version;       /* WQ_ABI_VERSION of the library */
+    int compiled_sm;       /* 100 for sm_100a */
+    int device;            /* device queried */
+    int device_cc;         /* major*10 + minor of that device */
+    int sm_count;          /* multiprocessors on that device */
+    int tcgen05;           /* 1 if the tcgen05 tensor-core path is built in */
+    char device_name[96];
+} wq_kernel_info_t;
+#define WQ_ABI_VERSION 1
+WQ_API int wq_kernel_info(int device, wq_kernel_info_t* out);
+
+/* ------------------------------------------------------------------------ */
+/* Dequant-GEMM: replaces `_kernels.dequant_gemm(x, q, scales, zeros,        */
+/* channel_scale, group_size, bits, nthreads)` (dequant_gemm.cpp:222-300,    */
+/* _kernels.pyi:3-12). `nthreads` has no counterpart: the launch shape is    */
+/* chosen from the problem. The array shapes are passed so that the same     */
+/* validation as the reference runs here (q is [M, q_cols], scales is        */
+/* [scale_rows, groups], zeros is [zero_rows, zero_groups], channel_scale is */
+/* [channel_len] or NULL with channel_len = -1). y is [B, M] with row        */
+/* stride ldy >= M elements (ldy = M for a dense output).                    */
+/* ------------------------------------------------------------------------ */
+WQ_API size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits);
+
+WQ_API int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
+                        const uint8_t* q, int64_t M, int64_t q_cols,
+                        const float* scales, int64_t scale_rows, int64_t groups,
+                        const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                        const float* channel_scale, int64_t channel_len,
+                        int group_size, int bits,
+                        float* y, int64_t ldy,
+                        void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* RTN quantize + pack: replaces `quantize_weight(weight, config,            */
+/* pre_scale=)` (quant.py:225-289) up to and including assemble_quantized's  */
+/* packing (quant.py:187-222, pack.py:17-33), bit for bit.                   */
+/*   w          fp32 [M, K] device                                           */
+/*   pre_scale  fp32 [K] or NULL (AWQ fold: quantizes w*s, writes 1/s)       */
+/*   group_mode > 0: group size; 0: per-tensor; -1: per-channel (None)       */
+/*   q_out      uint8 [M, (K+1)/2] (bits 4) or [M, K] (bits 8)               */
+/*   scales_out, zeros_out fp32 [rows, groups]: rows = 1 (tensor) or M,      */
+/*              groups = 1 (tensor/channel) or ceil(K / group_mode)          */
+/*   channel_out fp32 [K] (required iff pre_scale != NULL)                   */
+/*   flags      int32 [1] device word; the call zeroes it, and the kernels   */
+/*              OR in 1 (non-finite weight) or 2 (bad pre_scale). The caller */
+/*              reads it after the stream completes; nonzero means the       */
+/*              outputs are not valid (wq_rtn_flags_status maps it).         */
+/* ------------------------------------------------------------------------ */
+WQ_API size_t wq_rtn_workspace_bytes(int64_t M, int64_t K, int group_mode);
+WQ_API int wq_rtn_quantize_f32(const float* w, const float* pre_scale, int64_t M, int64_t K,
+                        int bits, int symmetric, int group_mode,
+                        uint8_t* q_out, float* scales_out, float* zeros_out,
+                        float* channel_out, int32_t* flags,
+                        void* workspace, size_t workspace_bytes, void* stream);
+/* WQ_OK for flags == 0, else the status of the first condition set. */
+WQ_API int wq_rtn_flags_status(int32_t flags);
+
+/* int4 packing (pack.py:17-33): codes int32 [M, K] -> packed uint8 [M, (K+1)/2].
+ * Range errors are reported through `minmax` (int32 [2] device: the call
+ * writes min and max of the codes; the caller raises WQ_E_INT4_RANGE if they
+ * fall outside [0, 15], as pack_int4 does). */
+WQ_API int wq_pack_int4(const int32_t* codes, int64_t M, int64_t K, uint8_t* packed,
+                 int32_t* minmax, void* stream);
+/* int4 unpacking (pack.py:36-55): packed uint8 [M, packed_cols] -> codes uint8 [M, K]. */
+WQ_API int wq_unpack_int4(const uint8_t* packed, int64_t M, int64_t packed_cols, int64_t K,
+                   uint8_t* codes, void* stream);
+
+/* Dense reconstruction W_hat fp32 [M, K] (quant.py:292-308, the operand of
+ * the reference's `impl="reference"` matmul, gemm.py:41-42). */
+WQ_API int wq_dequantize_f32(const uint8_t* q, int64_t M, int64_t K, int64_t q_cols,
+                      const float* scales, int64_t scale_rows, int64_t groups,
+                      const float* zeros, const float* channel_scale,
+                      int group_size, int bits, float* w_out, void* stream);
+
+/* Row-major [P, B, Mp] -> [B, P*Mp] permute, used after an all-gather of
+ * row-sharded outputs (each of P ranks produced y[:, p*Mp:(p+1)*Mp]). */
+WQ_API int wq_gather_permute_f32(const float* src, int64_t P, int64_t B, int64_t Mp,
+                          float* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WQ_B200_H */

@@ -1,0 +1,186 @@
+"""CPU oracle for the dequant-GEMM path (test infrastructure only).
+
+This package is the checker, never the thing measured or shipped: only the test
+suite, the smoke check and the benchmark's CPU-baseline leg import it. The
+product package does not import it and has no CPU fallback.
+
+Two implementations live here:
+
+* ``liboracle.so`` (``dq_oracle.c``): a plain-C restatement of ptqkit's CPU
+  dequant-GEMM (src/ptqkit/csrc/dequant_gemm.cpp:57-218), RTN quantizer
+  (src/ptqkit/quant.py:146-184, 225-289) and int4 packing (src/ptqkit/pack.py:17-55).
+* ``_ref/_kernels*.so``: ptqkit's own C++ kernel compiled from its single source
+  file by ``oracle/Makefile`` (target ``ref``). Present only where it was built.
+
+Both are pinned against outputs of the reference itself in ``tests/golden``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import glob
+import importlib.util
+import os
+import subprocess
+import sysconfig
+from types import ModuleType
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+_lib: ctypes.CDLL | None = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+def build(with_ref: bool = False) -> None:
+    """Compile the C oracle (and, if asked and its source is mounted, the reference kernel)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if with_ref:
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        handle = ctypes.CDLL(_LIB_PATH)
+        handle.orc_dequant_gemm.restype = ctypes.c_int
+        handle.orc_dequant_gemm.argtypes = [
+            _f32p, _u8p, _f32p, _f32p, _f32p, _f32p,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ]
+        handle.orc_rtn_quantize.restype = ctypes.c_int
+        handle.orc_rtn_quantize.argtypes = [
+            _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int, _i32p, _f32p, _f32p, _f32p,
+        ]
+        handle.orc_pack_int4.restype = ctypes.c_int
+        handle.orc_pack_int4.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, _u8p]
+        handle.orc_unpack_int4.restype = None
+        handle.orc_unpack_int4.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p]
+        _lib = handle
+    return _lib
+
+
+def _ptr(a: np.ndarray | None, kind: type) -> ctypes._Pointer | None:  # type: ignore[type-arg]
+    if a is None:
+        return None
+    return a.ctypes.data_as(ctypes.POINTER(kind))
+
+
+def _c(a: np.ndarray, dtype: type) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def dequant_gemm(
+    x: np.ndarray,
+    q: np.ndarray,
+    scales: np.ndarray,
+    zeros: np.ndarray,
+    channel_scale: np.ndarray | None,
+    group_size: int,
+    bits: int,
+    nthreads: int = 0,
+) -> np.ndarray:
+    """y = x @ W_hat^T, bitwise equal to ptqkit's AVX2 CPU kernel."""
+    x = _c(x, np.float32)
+    q = _c(q, np.uint8)
+    scales = _c(scales, np.float32)
+    zeros = _c(zeros, np.float32)
+    ch = None if channel_scale is None else _c(channel_scale, np.float32)
+    B, K = x.shape
+    M = q.shape[0]
+    y = np.zeros((B, M), dtype=np.float32)
+    rc = lib().orc_dequant_gemm(
+        _ptr(x, ctypes.c_float), _ptr(q, ctypes.c_uint8), _ptr(scales, ctypes.c_float),
+        _ptr(zeros, ctypes.c_float), _ptr(ch, ctypes.c_float), _ptr(y, ctypes.c_float),
+        B, M, K, scales.shape[0], scales.shape[1], group_size, bits, nthreads,
+    )
+    if rc != 0:
+        raise ValueError(f"oracle dequant_gemm rejected its arguments (status {rc})")
+    return y
+
+
+def rtn_quantize(
+    w: np.ndarray,
+    bits: int,
+    symmetric: bool,
+    group_size: int | None,
+    pre_scale: np.ndarray | None = None,
+) -> dict[str, np.ndarray | int]:
+    """RTN of quant.py:225-289. Returns int32 codes, fp32 scales/zeros, the stored
+    group_size (K for tensor and channel granularity) and the channel scale."""
+    w = _c(w, np.float32)
+    M, K = w.shape
+    if group_size is None:
+        mode, rows, groups, stored = -1, M, 1, K
+    elif group_size == 0:
+        mode, rows, groups, stored = 0, 1, 1, K
+    else:
+        mode, rows, groups, stored = group_size, M, (K + group_size - 1) // group_size, group_size
+    codes = np.zeros((M, K), dtype=np.int32)
+    scales = np.zeros((rows, groups), dtype=np.float32)
+    zeros = np.zeros((rows, groups), dtype=np.float32)
+    pre = None if pre_scale is None else _c(pre_scale, np.float32)
+    channel = None if pre is None else np.zeros(K, dtype=np.float32)
+    rc = lib().orc_rtn_quantize(
+        _ptr(w, ctypes.c_float), _ptr(pre, ctypes.c_float), M, K, bits, int(symmetric), mode,
+        _ptr(codes, ctypes.c_int32), _ptr(scales, ctypes.c_float), _ptr(zeros, ctypes.c_float),
+        _ptr(channel, ctypes.c_float),
+    )
+    if rc == 2:
+        raise ValueError("weight must be finite")
+    if rc == 3:
+        raise ValueError("pre_scale must be finite and positive")
+    if rc != 0:
+        raise ValueError(f"oracle rtn_quantize rejected its arguments (status {rc})")
+    return {"codes": codes, "scales": scales, "zeros": zeros, "group_size": stored, "channel_scale": channel}
+
+
+def pack_int4(codes: np.ndarray) -> np.ndarray:
+    codes = _c(codes, np.int32)
+    M, K = codes.shape
+    out = np.zeros((M, (K + 1) // 2), dtype=np.uint8)
+    if lib().orc_pack_int4(_ptr(codes, ctypes.c_int32), M, K, _ptr(out, ctypes.c_uint8)) != 0:
+        raise ValueError("int4 codes must lie in [0, 15]")
+    return out
+
+
+def unpack_int4(packed: np.ndarray, in_features: int) -> np.ndarray:
+    packed = _c(packed, np.uint8)
+    M = packed.shape[0]
+    out = np.zeros((M, in_features), dtype=np.uint8)
+    lib().orc_unpack_int4(_ptr(packed, ctypes.c_uint8), M, in_features, _ptr(out, ctypes.c_uint8))
+    return out
+
+
+def quantize_stored(
+    w: np.ndarray, bits: int, symmetric: bool, group_size: int | None, pre_scale: np.ndarray | None = None
+) -> dict[str, np.ndarray | int]:
+    """RTN followed by the storage step of assemble_quantized (quant.py:187-222):
+    int4 codes packed, int8 codes as uint8."""
+    r = rtn_quantize(w, bits, symmetric, group_size, pre_scale)
+    codes = r["codes"]
+    assert isinstance(codes, np.ndarray)
+    r["q"] = pack_int4(codes) if bits == 4 else codes.astype(np.uint8)
+    return r
+
+
+def reference_kernels() -> ModuleType | None:
+    """ptqkit's own compiled CPU kernel module from ``_ref/``, or None if not built."""
+    suffix = sysconfig.get_config_var("EXT_SUFFIX")
+    paths = glob.glob(os.path.join(HERE, "_ref", "_kernels" + suffix))
+    if not paths:
+        return None
+    spec = importlib.util.spec_from_file_location("_kernels", paths[0])
+    if spec is None or spec.loader is None:
+        return None
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module

@@ -1,0 +1,187 @@
+"""Dequant-GEMM on the GPU against the oracle and the reference's golden outputs.
+
+Tolerance (written once, in conftest.assert_close_y): max|dy| <= 1e-4 * (1 + |y|)
+elementwise and relative Frobenius error <= 1e-5 against the reference kernel's
+outputs; the reference's own kernel-vs-dense check (tests/test_gemm.py:62,
+rtol = atol = 1e-4) is applied as well.
+"""
+
+from __future__ import annotations
+
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close_y, small_cases, workload_digests
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_t(a: np.ndarray, dev: torch.device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def run_kernel(wq, data, name: str, meta: dict, dev: torch.device, x: np.ndarray | None = None) -> np.ndarray:
+    xs = data[f"{name}.x"] if x is None else x
+    ch = data.get(f"{name}.channel")
+    y = wq._kernels.dequant_gemm(
+        dev_t(xs, dev), dev_t(data[f"{name}.q"], dev), dev_t(data[f"{name}.scales"], dev),
+        dev_t(data[f"{name}.zeros"], dev), None if ch is None else dev_t(ch, dev),
+        meta["stored_group"], meta["bits"], 0)
+    return y.cpu().numpy()
+
+
+def test_nibble_dot_known_answer(wq, cuda) -> None:
+    # tests/test_gemm.py:13-32, through the package's own packing and both impls
+    codes = torch.tensor([[1, 2], [15, 0]], dtype=torch.int32, device=cuda)
+    qw = wq.assemble_quantized(codes, torch.tensor([[1.0], [1.0]]), torch.zeros(2, 1), bits=4,
+                               group_size=2, symmetric=True, granularity="channel")
+    x = torch.tensor([[1.0, 0.0], [0.0, 1.0], [1.0, 1.0]], device=cuda)
+    expect = torch.tensor([[1.0, 15.0], [2.0, 0.0], [3.0, 15.0]], device=cuda)
+    assert torch.allclose(wq.dequant_gemm(x, qw, impl="reference"), expect, atol=1e-6)
+    assert torch.allclose(wq.dequant_gemm(x, qw, impl="kernel"), expect, atol=1e-6)
+
+
+def test_golden_cases(wq, cuda) -> None:
+    data, meta = small_cases()
+    rtn = {m["name"]: m for m in meta if m["kind"] in ("rtn", "kat")}
+    n = 0
+    for m in meta:
+        if m["kind"] != "gemm":
+            continue
+        name = m["name"]
+        got = run_kernel(wq, data, name, rtn[name], cuda)
+        assert_close_y(got, data[f"{name}.y_kernel"], name)
+        assert np.allclose(got, data[f"{name}.y_reference"], rtol=1e-4, atol=1e-4), name
+        n += 1
+    assert n > 30
+
+
+def test_reference_test_cases_through_package(wq, cuda) -> None:
+    """tests/test_gemm.py:35-65 run through the package API end to end (GPU RTN + GPU GEMM)."""
+    cases = [
+        (4, 8, 1, 8, True, None, False), (5, 7, 3, 8, True, 0, False), (8, 16, 4, 4, True, 8, False),
+        (3, 13, 1, 4, False, 4, False), (6, 32, 5, 4, True, 16, True), (32, 128, 2, 4, True, 128, False),
+        (4, 1, 2, 8, True, None, False), (7, 17, 8, 8, False, None, False),
+    ]
+    data, _ = small_cases()
+    g = torch.Generator().manual_seed(0)
+    for i, (out, inn, batch, bits, sym, group, use_pre) in enumerate(cases):
+        w = torch.randn(out, inn, generator=g)
+        pre = torch.rand(inn, generator=g) + 0.25 if use_pre else None
+        qw = wq.quantize_weight(w, wq.QuantConfig(bits=bits, symmetric=sym, group_size=group), pre_scale=pre)
+        x = torch.randn(batch, inn, generator=g).to(cuda)
+        ref = wq.dequant_gemm(x, qw, impl="reference")
+        got = wq.dequant_gemm(x, qw, impl="kernel", nthreads=1)
+        assert torch.allclose(got, ref, rtol=1e-4, atol=1e-4), i
+        assert_close_y(got.cpu().numpy(), data[f"refcase{i}.y_kernel"], f"refcase{i}")
+        again = wq.dequant_gemm(x, qw, impl="kernel", nthreads=2)
+        assert torch.equal(got, again)
+
+
+def _rand_layer(wq, g, M, K, bits, sym, group, pre=False):
+    w = torch.randn(M, K, generator=g) * 0.02
+    s = torch.rand(K, generator=g) + 0.25 if pre else None
+    return wq.quantize_weight(w, wq.QuantConfig(bits=bits, symmetric=sym, group_size=group), pre_scale=s)
+
+
+def _oracle_y(orc, qw, x: torch.Tensor) -> np.ndarray:
+    ch = None if qw.channel_scale is None else qw.channel_scale.cpu().numpy()
+    return orc.dequant_gemm(x.cpu().numpy(), qw.codes.cpu().numpy(), qw.scales.cpu().numpy(),
+                            qw.zeros.cpu().numpy(), ch, qw.group_size, qw.bits)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 17])
+def test_shapes_sweep_vs_oracle(wq, orc, cuda, bits: int, batch: int) -> None:
+    """Decode-path and tiled-path shapes: odd K, odd groups, per-tensor broadcast,
+    channel scale, rows not a multiple of any tile."""
+    g = torch.Generator().manual_seed(100 + bits * 10 + batch)
+    shapes = [(96, 256, 128, True, False), (130, 1024, 64, False, True), (33, 4095, 64, True, False),
+              (64, 768, None, False, False), (50, 300, 0, True, False), (17, 13, 3, False, False),
+              (40, 2048, 32, True, True), (257, 512, 512, False, False)]
+    for (M, K, group, sym, pre) in shapes:
+        qw = _rand_layer(wq, g, M, K, bits, sym, group, pre)
+        x = torch.randn(batch, K, generator=g)
+        got = wq.dequant_gemm(x.to(cuda), qw, impl="kernel").cpu().numpy()
+        assert_close_y(got, _oracle_y(orc, qw, x), f"{M}x{K} g{group} b{batch} bits{bits}")
+
+
+def test_decode_and_tiled_paths_agree(wq, orc, cuda) -> None:
+    """The same problem through the streaming kernel (aligned rows) and through
+    the tiled kernel (a copy of the codes at a 1-byte offset, which the
+    streaming kernel does not take)."""
+    g = torch.Generator().manual_seed(5)
+    for bits in (4, 8):
+        qw = _rand_layer(wq, g, 300, 2048, bits, True, 128)
+        x = torch.randn(3, 2048, generator=g).to(cuda)
+        y_fast = wq._kernels.dequant_gemm(x, qw.codes, qw.scales, qw.zeros, None, qw.group_size, bits)
+        buf = torch.empty(qw.codes.numel() + 16, dtype=torch.uint8, device=cuda)
+        shifted = buf[1:1 + qw.codes.numel()].view(qw.codes.shape)
+        shifted.copy_(qw.codes)
+        assert shifted.data_ptr() % 16 != 0
+        y_tiled = wq._kernels.dequant_gemm(x, shifted, qw.scales, qw.zeros, None, qw.group_size, bits)
+        ref = _oracle_y(orc, qw, x)
+        assert_close_y(y_fast.cpu().numpy(), ref, "fast")
+        assert_close_y(y_tiled.cpu().numpy(), ref, "tiled")
+
+
+def test_deterministic_repeat(wq, cuda) -> None:
+    g = torch.Generator().manual_seed(9)
+    qw = _rand_layer(wq, g, 1000, 4096, 4, True, 128)
+    for b in (1, 4, 64):
+        x = torch.randn(b, 4096, generator=g).to(cuda)
+        a = wq.dequant_gemm(x, qw, impl="kernel")
+        c = wq.dequant_gemm(x, qw, impl="kernel")
+        assert torch.equal(a, c)
+
+
+def test_edge_sizes(wq, cuda) -> None:
+    g = torch.Generator().manual_seed(11)
+    qw = _rand_layer(wq, g, 8, 64, 4, True, 32)
+    # empty batch
+    y = wq.dequant_gemm(torch.zeros(0, 64, device=cuda), qw, impl="kernel")
+    assert y.shape == (0, 8)
+    # leading dims are kept
+    x = torch.randn(2, 3, 64, generator=g).to(cuda)
+    y = wq.dequant_gemm(x, qw, impl="kernel")
+    assert y.shape == (2, 3, 8)
+    assert torch.allclose(y, wq.dequant_gemm(x, qw, impl="reference"), rtol=1e-4, atol=1e-4)
+    # all-zero activations and activations with a huge dynamic range
+    for xs in (torch.zeros(2, 64), torch.tensor([[1e30] + [1e-30] * 63, [3.0] * 64])):
+        y = wq.dequant_gemm(xs.to(cuda), qw, impl="kernel")
+        r = wq.dequant_gemm(xs.to(cuda), qw, impl="reference")
+        assert torch.allclose(y, r, rtol=1e-5, atol=1e-30)
+
+
+def test_output_into_strided_view(wq, cuda) -> None:
+    g = torch.Generator().manual_seed(12)
+    qw = _rand_layer(wq, g, 96, 512, 4, True, 128)
+    x = torch.randn(2, 512, generator=g).to(cuda)
+    big = torch.full((2, 200), -7.0, device=cuda)
+    view = big[:, 50:146]
+    wq._kernels.dequant_gemm(x, qw.codes, qw.scales, qw.zeros, None, qw.group_size, 4, out=view)
+    assert torch.allclose(view, wq.dequant_gemm(x, qw, impl="reference"), rtol=1e-4, atol=1e-4)
+    assert torch.all(big[:, :50] == -7.0) and torch.all(big[:, 146:] == -7.0)
+
+
+@pytest.mark.parametrize("wname", ["gpt2_c_fc_int4_g128", "gpt2_small_int8_asym", "awq_11008x4096",
+                                   "oddk_4096x4095_g64", "sharded_28672x8192"])
+def test_workloads_vs_oracle(wq, orc, cuda, wname: str) -> None:
+    wl = importlib.import_module("weight-quantizer_b200.workloads")
+    layers = wl.WORKLOADS[wname]()
+    dig = workload_digests()[wname]
+    sample = torch.Generator().manual_seed(3)
+    for layer, d in zip(layers, dig):
+        qw = wq.quantize_weight(layer.weight, layer.config, pre_scale=layer.pre_scale)
+        for b, x in layer.x.items():
+            got = wq.dequant_gemm(x.to(cuda), qw, impl="kernel").cpu()
+            if b <= 256:
+                ref = _oracle_y(orc, qw, x)
+                assert_close_y(got.numpy(), ref, f"{wname}/{layer.name} b{b}")
+            else:
+                rows = torch.randperm(b, generator=sample)[:64]
+                ref = _oracle_y(orc, qw, x[rows])
+                assert_close_y(got[rows].numpy(), ref, f"{wname}/{layer.name} b{b} sampled rows")

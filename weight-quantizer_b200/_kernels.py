@@ -1,0 +1,328 @@
+"""ctypes binding of ``libwq_b200.so``, the counterpart of ptqkit's native module.
+
+ptqkit's ``_kernels`` (src/ptqkit/_kernels.pyi:3-12, src/ptqkit/csrc/dequant_gemm.cpp:317-331)
+exposes ``dequant_gemm(x, q, scales, zeros, channel_scale, group_size, bits, nthreads)``
+and ``kernel_info()``. This module exposes the same two with the same argument
+names and error behaviour (``ValueError`` with the reference's messages for bad
+arguments), operating on CUDA tensors through the library's C ABI
+(``include/wq_b200.h``), plus the device RTN, packing and reconstruction entry points.
+
+PyTorch only supplies device memory and the current stream. There is no CPU
+path: if the library is missing, every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Any
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libwq_b200.so")
+
+WQ_OK = 0
+WQ_E_CUDA = 14
+_ARG_ERRORS_AS_VALUEERROR = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15, 16, 17, 18, 19, 20}
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol declared in include/wq_b200.h
+SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "wq_status_string": (ctypes.c_char_p, [_int]),
+    "wq_last_cuda_error": (ctypes.c_char_p, []),
+    "wq_kernel_info": (_int, [_int, _vp]),
+    "wq_dequant_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
+    "wq_dequant_gemm_f32": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
+         _int, _int, _vp, _i64, _vp, _sz, _vp],
+    ),
+    "wq_rtn_workspace_bytes": (_sz, [_i64, _i64, _int]),
+    "wq_rtn_quantize_f32": (
+        _int,
+        [_vp, _vp, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "wq_rtn_flags_status": (_int, [ctypes.c_int32]),
+    "wq_pack_int4": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "wq_unpack_int4": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "wq_dequantize_f32": (
+        _int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _int, _int, _vp, _vp]
+    ),
+    "wq_gather_permute_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+}
+
+
+class _KernelInfo(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_int),
+        ("compiled_sm", ctypes.c_int),
+        ("device", ctypes.c_int),
+        ("device_cc", ctypes.c_int),
+        ("sm_count", ctypes.c_int),
+        ("tcgen05", ctypes.c_int),
+        ("device_name", ctypes.c_char * 96),
+    ]
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def library() -> ctypes.CDLL:
+    """Load the in-tree C-ABI library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"wq_b200 CUDA library not found at {LIB_PATH}; build it with "
+                "`make -C weight-quantizer_b200/csrc` (or __graft_entry__.build())"
+            )
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def status_message(status: int) -> str:
+    msg: bytes = library().wq_status_string(status)
+    return msg.decode()
+
+
+def _check(status: int) -> None:
+    if status == WQ_OK:
+        return
+    if status == WQ_E_CUDA:
+        detail: bytes = library().wq_last_cuda_error()
+        raise RuntimeError(f"wq_b200: {detail.decode()}")
+    if status in _ARG_ERRORS_AS_VALUEERROR:
+        raise ValueError(status_message(status))
+    raise RuntimeError(f"wq_b200: status {status}")
+
+
+def _stream(device: torch.device) -> int:
+    return int(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else int(t.data_ptr())
+
+
+def _cuda_device(tensors: list[torch.Tensor]) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise ValueError("dequant kernel inputs must be CUDA tensors")
+        if t.device != dev:
+            raise ValueError("dequant kernel inputs must be on one CUDA device")
+    return dev
+
+
+def kernel_info(device: int | None = None) -> dict[str, Any]:
+    """Build and device facts (counterpart of ``_kernels.kernel_info``)."""
+    if device is None:
+        device = torch.cuda.current_device() if torch.cuda.is_available() else 0
+    info = _KernelInfo()
+    status = library().wq_kernel_info(int(device), ctypes.byref(info))
+    out: dict[str, Any] = {
+        "abi_version": info.abi_version,
+        "arch": f"sm_{info.compiled_sm}a",
+        "tcgen05": bool(info.tcgen05),
+    }
+    if status == WQ_OK:
+        out.update(device=info.device_name.decode(), device_cc=info.device_cc, sm_count=info.sm_count)
+    return out
+
+
+def dequant_gemm(
+    x: torch.Tensor,
+    q: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    channel_scale: torch.Tensor | None,
+    group_size: int,
+    bits: int,
+    nthreads: int = 0,
+    *,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y[B, M] = x[B, K] @ W_hat^T on the current CUDA stream.
+
+    Same arguments as ptqkit's ``_kernels.dequant_gemm``. Inputs are cast to
+    fp32/uint8 and made contiguous like the reference's ``forcecast | c_style``
+    arrays (dequant_gemm.cpp:223-226). ``nthreads`` is accepted and ignored.
+    ``out`` may be a preallocated fp32 [B, M] view with unit column stride.
+    """
+    del nthreads
+    if x.ndim != 2:
+        raise ValueError("x must have shape [B, K]")
+    if q.ndim != 2 or scales.ndim != 2 or zeros.ndim != 2:
+        raise ValueError("q, scales, and zeros must be rank 2")
+    tensors = [x, q, scales, zeros] + ([] if channel_scale is None else [channel_scale])
+    dev = _cuda_device(tensors)
+    x = x.to(dtype=torch.float32).contiguous()
+    q = q.to(dtype=torch.uint8).contiguous()
+    scales = scales.to(dtype=torch.float32).contiguous()
+    zeros = zeros.to(dtype=torch.float32).contiguous()
+    ch_len = -1
+    if channel_scale is not None:
+        channel_scale = channel_scale.to(dtype=torch.float32).contiguous()
+        if channel_scale.ndim != 1:
+            raise ValueError("channel_scale must have shape [K]")
+        ch_len = int(channel_scale.shape[0])
+    B, K = int(x.shape[0]), int(x.shape[1])
+    M = int(q.shape[0])
+    if out is None:
+        y = torch.empty((B, M), dtype=torch.float32, device=dev)
+        ldy = M
+    else:
+        if out.dtype != torch.float32 or out.device != dev or tuple(out.shape) != (B, M):
+            raise ValueError("out must be a float32 [B, M] tensor on the inputs' device")
+        if M > 0 and B > 1 and out.stride(1) != 1:
+            raise ValueError("out must have unit column stride")
+        y = out
+        ldy = int(out.stride(0)) if B > 1 else M
+    lib = library()
+    ws_bytes = int(lib.wq_dequant_gemm_workspace_bytes(B, M, K, int(group_size), int(bits)))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    status = lib.wq_dequant_gemm_f32(
+        _ptr(x), B, K,
+        _ptr(q), M, int(q.shape[1]),
+        _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
+        _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
+        _ptr(channel_scale), ch_len,
+        int(group_size), int(bits),
+        _ptr(y), ldy,
+        _ptr(ws), ws_bytes,
+        _stream(dev),
+    )
+    _check(status)
+    return y
+
+
+def rtn_quantize(
+    w: torch.Tensor,
+    bits: int,
+    symmetric: bool,
+    group_mode: int,
+    pre_scale: torch.Tensor | None = None,
+) -> dict[str, torch.Tensor]:
+    """Device RTN + pack. ``group_mode``: >0 group size, 0 per-tensor, -1 per-channel.
+
+    Returns stored codes (packed for int4), fp32 scales/zeros and, with
+    ``pre_scale``, the stored channel scale 1/s. Reads the status flags back
+    (one host synchronization), as the reference raises before returning."""
+    if w.ndim != 2:
+        raise ValueError("weight must have shape [out, in]")
+    dev = _cuda_device([w] + ([] if pre_scale is None else [pre_scale]))
+    w = w.to(dtype=torch.float32).contiguous()
+    M, K = int(w.shape[0]), int(w.shape[1])
+    if pre_scale is not None:
+        pre_scale = pre_scale.to(dtype=torch.float32).reshape(-1).contiguous()
+        if int(pre_scale.numel()) != K:
+            raise ValueError("pre_scale must have one entry per input channel")
+    if group_mode > 0:
+        rows, groups = M, (K + group_mode - 1) // group_mode
+    elif group_mode == 0:
+        rows, groups = 1, 1
+    else:
+        rows, groups = M, 1
+    cols = (K + 1) // 2 if bits == 4 else K
+    q = torch.empty((M, cols), dtype=torch.uint8, device=dev)
+    scales = torch.empty((rows, groups), dtype=torch.float32, device=dev)
+    zeros = torch.empty((rows, groups), dtype=torch.float32, device=dev)
+    channel = torch.empty(K, dtype=torch.float32, device=dev) if pre_scale is not None else None
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = library()
+    ws_bytes = int(lib.wq_rtn_workspace_bytes(M, K, int(group_mode)))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    status = lib.wq_rtn_quantize_f32(
+        _ptr(w), _ptr(pre_scale), M, K, int(bits), int(bool(symmetric)), int(group_mode),
+        _ptr(q), _ptr(scales), _ptr(zeros), _ptr(channel), _ptr(flags), _ptr(ws), ws_bytes,
+        _stream(dev),
+    )
+    _check(status)
+    _check(int(lib.wq_rtn_flags_status(int(flags.item()))))
+    out = {"codes": q, "scales": scales, "zeros": zeros}
+    if channel is not None:
+        out["channel_scale"] = channel
+    return out
+
+
+def pack_int4(codes: torch.Tensor) -> torch.Tensor:
+    """codes [M, K] in [0, 15] -> packed uint8 [M, ceil(K/2)] (pack.py:17-33)."""
+    if codes.ndim != 2:
+        raise ValueError("codes must have shape [M, K]")
+    dev = _cuda_device([codes])
+    c = codes.to(dtype=torch.int32).contiguous()
+    M, K = int(c.shape[0]), int(c.shape[1])
+    packed = torch.empty((M, (K + 1) // 2), dtype=torch.uint8, device=dev)
+    mm = torch.empty(2, dtype=torch.int32, device=dev)
+    _check(library().wq_pack_int4(_ptr(c), M, K, _ptr(packed), _ptr(mm), _stream(dev)))
+    if M * K > 0:
+        lo, hi = (int(v) for v in mm.tolist())
+        if lo < 0 or hi > 15:
+            raise ValueError(f"int4 codes must lie in [0, 15], got [{lo}, {hi}]")
+    return packed
+
+
+def unpack_int4(packed: torch.Tensor, in_features: int) -> torch.Tensor:
+    """Invert pack_int4 and drop the pad nibble (pack.py:36-55)."""
+    if packed.ndim != 2 or packed.dtype != torch.uint8:
+        raise ValueError("packed int4 storage must be a uint8 matrix")
+    if in_features < 0:
+        raise ValueError("in_features must be non-negative")
+    need = (in_features + 1) // 2
+    if packed.shape[1] < need:
+        raise ValueError("packed row is shorter than in_features")
+    dev = _cuda_device([packed])
+    p = packed.contiguous()
+    M = int(p.shape[0])
+    out = torch.empty((M, in_features), dtype=torch.uint8, device=dev)
+    _check(library().wq_unpack_int4(_ptr(p), M, int(p.shape[1]), int(in_features), _ptr(out), _stream(dev)))
+    return out
+
+
+def dequantize(
+    q: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    channel_scale: torch.Tensor | None,
+    in_features: int,
+    group_size: int,
+    bits: int,
+) -> torch.Tensor:
+    """W_hat fp32 [M, K] exactly as quant.py:292-308 computes it."""
+    dev = _cuda_device([q, scales, zeros] + ([] if channel_scale is None else [channel_scale]))
+    q = q.contiguous()
+    scales = scales.to(dtype=torch.float32).contiguous()
+    zeros = zeros.to(dtype=torch.float32).contiguous()
+    if channel_scale is not None:
+        channel_scale = channel_scale.to(dtype=torch.float32).contiguous()
+    M, K = int(q.shape[0]), int(in_features)
+    out = torch.empty((M, K), dtype=torch.float32, device=dev)
+    _check(
+        library().wq_dequantize_f32(
+            _ptr(q), M, K, int(q.shape[1]), _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
+            _ptr(zeros), _ptr(channel_scale), int(group_size), int(bits), _ptr(out), _stream(dev),
+        )
+    )
+    return out
+
+
+def gather_permute(src: torch.Tensor, parts: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[P, B, Mp] (row-sharded outputs stacked by rank) -> [B, P*Mp]."""
+    dev = _cuda_device([src])
+    P, B, Mp = int(src.shape[0]), int(src.shape[1]), int(src.shape[2])
+    if P != parts:
+        raise ValueError("leading dimension must equal the number of parts")
+    s = src.contiguous()
+    dst = out if out is not None else torch.empty((B, P * Mp), dtype=torch.float32, device=dev)
+    _check(library().wq_gather_permute_f32(_ptr(s), P, B, Mp, _ptr(dst), _stream(dev)))
+    return dst

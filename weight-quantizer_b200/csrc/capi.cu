@@ -1,0 +1,244 @@
+// C ABI entry points (include/wq_b200.h): argument validation in the order and
+// with the messages of ptqkit's pybind11 entry point
+// (src/ptqkit/csrc/dequant_gemm.cpp:222-300), then dispatch to the kernels.
+// Nothing here allocates device memory or synchronizes the host.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/wq_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wq {
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+}  // namespace wq
+
+namespace {
+
+thread_local char g_cuda_error[256] = "no error";
+
+int cuda_fail(cudaError_t e) {
+    std::snprintf(g_cuda_error, sizeof(g_cuda_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+    return WQ_E_CUDA;
+}
+
+constexpr int64_t kMaxDim = ((int64_t)1 << 31) - 1;
+
+}  // namespace
+
+extern "C" {
+
+const char* wq_status_string(int status) {
+    switch (status) {
+        case WQ_OK: return "ok";
+        case WQ_E_X_SHAPE: return "x must have shape [B, K]";
+        case WQ_E_RANK: return "q, scales, and zeros must be rank 2";
+        case WQ_E_BITS: return "bits must be 4 or 8";
+        case WQ_E_GROUP_SIZE: return "group_size must be positive";
+        case WQ_E_NEG_DIM: return "negative dimension";
+        case WQ_E_PACKED_COLS: return "packed code row length does not match K";
+        case WQ_E_ZEROS_SHAPE: return "zeros shape must match scales";
+        case WQ_E_SCALE_ROWS: return "scale rows must be 1 or M";
+        case WQ_E_SCALE_GROUPS: return "scale groups must equal ceil(K / group_size)";
+        case WQ_E_CHANNEL_SHAPE: return "channel_scale must have shape [K]";
+        case WQ_E_NULL: return "a required device pointer is null";
+        case WQ_E_WORKSPACE: return "workspace is smaller than the size the workspace query returned";
+        case WQ_E_TOO_LARGE: return "a dimension exceeds the range the kernels index";
+        case WQ_E_CUDA: return "CUDA error (see wq_last_cuda_error)";
+        case WQ_E_NOT_FINITE: return "weight must be finite";
+        case WQ_E_PRE_SCALE_LEN: return "pre_scale must have one entry per input channel";
+        case WQ_E_PRE_SCALE_VAL: return "pre_scale must be finite and positive";
+        case WQ_E_INT4_RANGE: return "int4 codes must lie in [0, 15]";
+        case WQ_E_GROUP_MODE: return "group_size must be None, 0, or positive";
+        case WQ_E_LD: return "output row stride is smaller than the output row length";
+        default: return "unknown status";
+    }
+}
+
+const char* wq_last_cuda_error(void) { return g_cuda_error; }
+
+int wq_kernel_info(int device, wq_kernel_info_t* out) {
+    if (out == nullptr) return WQ_E_NULL;
+    std::memset(out, 0, sizeof(*out));
+    out->abi_version = WQ_ABI_VERSION;
+    out->compiled_sm = 100;
+    out->device = device;
+    out->tcgen05 = 0;
+    cudaDeviceProp prop;
+    cudaError_t e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(e);
+    out->device_cc = prop.major * 10 + prop.minor;
+    out->sm_count = prop.multiProcessorCount;
+    std::snprintf(out->device_name, sizeof(out->device_name), "%s", prop.name);
+    return WQ_OK;
+}
+
+size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
+    (void)M;
+    (void)group_size;
+    if (B <= 0 || K <= 0 || (bits != 4 && bits != 8)) return 0;
+    if (B <= wq::kGemvMaxBatch) return wq::gemv_workspace_bytes(B, K, bits);
+    return 0;
+}
+
+int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
+                        const uint8_t* q, int64_t M, int64_t q_cols,
+                        const float* scales, int64_t scale_rows, int64_t groups,
+                        const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                        const float* channel_scale, int64_t channel_len,
+                        int group_size, int bits,
+                        float* y, int64_t ldy,
+                        void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    // dequant_gemm.cpp:241-276, same order
+    if (bits != 4 && bits != 8) return WQ_E_BITS;
+    if (group_size <= 0) return WQ_E_GROUP_SIZE;
+    if (K < 0 || M < 0 || B < 0) return WQ_E_NEG_DIM;
+    const int64_t packed_cols = bits == 4 ? (K + 1) / 2 : K;
+    if (q_cols != packed_cols) return WQ_E_PACKED_COLS;
+    if (zero_rows != scale_rows || zero_groups != groups) return WQ_E_ZEROS_SHAPE;
+    if (scale_rows != 1 && scale_rows != M) return WQ_E_SCALE_ROWS;
+    const int64_t n_groups = K == 0 ? 0 : (K + group_size - 1) / group_size;
+    if (K > 0 && groups != n_groups) return WQ_E_SCALE_GROUPS;
+    if (channel_scale != nullptr && channel_len != K) return WQ_E_CHANNEL_SHAPE;
+    // beyond the reference: output stride, pointers, index range
+    if (ldy < M) return WQ_E_LD;
+    if (B > kMaxDim || M > kMaxDim || K > kMaxDim || groups > kMaxDim) return WQ_E_TOO_LARGE;
+    if (B == 0 || M == 0) return WQ_OK;
+    if (y == nullptr) return WQ_E_NULL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        cudaError_t e = wq::launch_fill_zero(y, B, M, ldy, s);
+        return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+    }
+    if (x == nullptr || q == nullptr || scales == nullptr || zeros == nullptr) return WQ_E_NULL;
+
+    wq::GemmProblem p;
+    p.x = x;
+    p.q = q;
+    p.scales = scales;
+    p.zeros = zeros;
+    p.channel = channel_scale;
+    p.y = y;
+    p.B = B;
+    p.M = M;
+    p.K = K;
+    p.q_stride = q_cols;
+    p.ldy = ldy;
+    p.scale_rows = (int)scale_rows;
+    p.groups = (int)groups;
+    p.group_size = group_size;
+    p.bits = bits;
+
+    cudaError_t e;
+    if (wq::gemv_supported(p)) {
+        const size_t need = wq::gemv_workspace_bytes(B, K, bits);
+        if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
+        e = wq::launch_gemv(p, workspace, s);
+    } else {
+        e = wq::launch_gemm_simt(p, s);
+    }
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+size_t wq_rtn_workspace_bytes(int64_t M, int64_t K, int group_mode) {
+    return wq::rtn_workspace_bytes(M, K, group_mode);
+}
+
+int wq_rtn_flags_status(int32_t flags) {
+    if (flags & 1) return WQ_E_NOT_FINITE;
+    if (flags & 2) return WQ_E_PRE_SCALE_VAL;
+    return WQ_OK;
+}
+
+int wq_rtn_quantize_f32(const float* w, const float* pre_scale, int64_t M, int64_t K,
+                        int bits, int symmetric, int group_mode,
+                        uint8_t* q_out, float* scales_out, float* zeros_out,
+                        float* channel_out, int32_t* flags,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+    if (bits != 4 && bits != 8) return WQ_E_BITS;
+    if (group_mode < -1) return WQ_E_GROUP_MODE;
+    if (M < 0 || K < 0) return WQ_E_NEG_DIM;
+    if (M > kMaxDim || K > kMaxDim || M * K > ((int64_t)1 << 62)) return WQ_E_TOO_LARGE;
+    if (K > 200 * 1024) return WQ_E_TOO_LARGE;
+    if (flags == nullptr) return WQ_E_NULL;
+    if (pre_scale != nullptr && channel_out == nullptr) return WQ_E_NULL;
+    if (M > 0 && K > 0 && (w == nullptr || q_out == nullptr || scales_out == nullptr || zeros_out == nullptr))
+        return WQ_E_NULL;
+    const size_t need = wq::rtn_workspace_bytes(M, K, group_mode);
+    if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
+    wq::RtnProblem p;
+    p.w = w;
+    p.pre_scale = pre_scale;
+    p.M = M;
+    p.K = K;
+    p.bits = bits;
+    p.symmetric = symmetric ? 1 : 0;
+    p.group_mode = group_mode;
+    p.q_out = q_out;
+    p.scales_out = scales_out;
+    p.zeros_out = zeros_out;
+    p.channel_out = channel_out;
+    p.flags = flags;
+    cudaError_t e = wq::launch_rtn(p, workspace, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_pack_int4(const int32_t* codes, int64_t M, int64_t K, uint8_t* packed, int32_t* minmax, void* stream) {
+    if (M < 0 || K < 0) return WQ_E_NEG_DIM;
+    if (minmax == nullptr) return WQ_E_NULL;
+    if (M > 0 && K > 0 && (codes == nullptr || packed == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_pack_int4(codes, M, K, packed, minmax, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_unpack_int4(const uint8_t* packed, int64_t M, int64_t packed_cols, int64_t K, uint8_t* codes,
+                   void* stream) {
+    if (M < 0 || K < 0) return WQ_E_NEG_DIM;
+    if (packed_cols < (K + 1) / 2) return WQ_E_PACKED_COLS;
+    if (M > 0 && K > 0 && (codes == nullptr || packed == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_unpack_int4(packed, M, packed_cols, K, codes, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_dequantize_f32(const uint8_t* q, int64_t M, int64_t K, int64_t q_cols,
+                      const float* scales, int64_t scale_rows, int64_t groups,
+                      const float* zeros, const float* channel_scale,
+                      int group_size, int bits, float* w_out, void* stream) {
+    if (bits != 4 && bits != 8) return WQ_E_BITS;
+    if (group_size <= 0) return WQ_E_GROUP_SIZE;
+    if (K < 0 || M < 0) return WQ_E_NEG_DIM;
+    const int64_t packed_cols = bits == 4 ? (K + 1) / 2 : K;
+    if (q_cols < packed_cols) return WQ_E_PACKED_COLS;
+    if (scale_rows != 1 && scale_rows != M) return WQ_E_SCALE_ROWS;
+    if (K > 0 && groups != (K + group_size - 1) / group_size) return WQ_E_SCALE_GROUPS;
+    if (M == 0 || K == 0) return WQ_OK;
+    if (q == nullptr || scales == nullptr || zeros == nullptr || w_out == nullptr) return WQ_E_NULL;
+    cudaError_t e = wq::launch_dequantize(q, M, K, q_cols, scales, (int)scale_rows, (int)groups, zeros,
+                                          channel_scale, group_size, bits, w_out,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_gather_permute_f32(const float* src, int64_t P, int64_t B, int64_t Mp, float* dst, void* stream) {
+    if (P < 0 || B < 0 || Mp < 0) return WQ_E_NEG_DIM;
+    if (P * B * Mp > 0 && (src == nullptr || dst == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_gather_permute(src, P, B, Mp, dst, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace wq {
+
+// One dequant-GEMM problem in ptqkit's storage layout (see include/wq_b200.h).
+struct GemmProblem {
+    const float* x;        // [B, K]
+    const uint8_t* q;      // [M, q_stride] bytes
+    const float* scales;   // [scale_rows, groups]
+    const float* zeros;    // [scale_rows, groups]
+    const float* channel;  // [K] or nullptr
+    float* y;              // [B, ldy]
+    int64_t B, M, K;
+    int64_t q_stride;      // bytes per stored row: K (int8) or (K+1)/2 (int4)
+    int64_t ldy;
+    int scale_rows, groups, group_size, bits;
+};
+
+// --- K1: streaming decode kernel (small batch, weight-stream bound) --------
+constexpr int kGemvMaxBatch = 4;
+// Workspace the decode path needs for this problem (0 if it does not apply).
+size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
+// True when the decode kernel can run this problem (alignment, group shape,
+// batch, shared-memory fit).
+bool gemv_supported(const GemmProblem& p);
+cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
+
+// --- generic tiled SIMT kernel: any shape, reference per-element formula ---
+cudaError_t launch_gemm_simt(const GemmProblem& p, cudaStream_t s);
+
+// --- zero-fill of y for K == 0 ---------------------------------------------
+cudaError_t launch_fill_zero(float* y, int64_t B, int64_t M, int64_t ldy, cudaStream_t s);
+
+// --- RTN quantize + pack -----------------------------------------------------
+struct RtnProblem {
+    const float* w;          // [M, K]
+    const float* pre_scale;  // [K] or nullptr
+    int64_t M, K;
+    int bits, symmetric, group_mode;  // group_mode: >0 group, 0 tensor, -1 channel
+    uint8_t* q_out;
+    float* scales_out;
+    float* zeros_out;
+    float* channel_out;
+    int32_t* flags;
+};
+size_t rtn_workspace_bytes(int64_t M, int64_t K, int group_mode);
+cudaError_t launch_rtn(const RtnProblem& p, void* workspace, cudaStream_t s);
+
+cudaError_t launch_pack_int4(const int32_t* codes, int64_t M, int64_t K, uint8_t* packed,
+                             int32_t* minmax, cudaStream_t s);
+cudaError_t launch_unpack_int4(const uint8_t* packed, int64_t M, int64_t packed_cols, int64_t K,
+                               uint8_t* codes, cudaStream_t s);
+cudaError_t launch_dequantize(const uint8_t* q, int64_t M, int64_t K, int64_t q_stride,
+                              const float* scales, int scale_rows, int groups,
+                              const float* zeros, const float* channel, int group_size, int bits,
+                              float* w_out, cudaStream_t s);
+cudaError_t launch_gather_permute(const float* src, int64_t P, int64_t B, int64_t Mp, float* dst,
+                                  cudaStream_t s);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace wq

@@ -1,0 +1,112 @@
+"""Row-sharded (column-parallel) dequant-GEMM across the GPUs of one node.
+
+ptqkit splits the output rows of a layer across OpenMP threads
+(src/ptqkit/csrc/dequant_gemm.cpp:196-205). Here the same split is taken across
+GPUs, one process per GPU: rank r owns rows [r*Mp, (r+1)*Mp) of the packed
+codes and of the scale/zero tables (Mp = ceil(M / world); the last shard is
+padded with rows whose output is dropped), while x and the channel scale are
+replicated. Each rank computes its y shard with the local kernel; when the
+whole y is needed, one NCCL all-gather over NVLink collects the shards as
+[world, B, Mp] and a permute kernel lays them out as [B, M]. Per-tensor
+granularity (one scale for all rows) is replicated on every rank.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _kernels
+from .quant import QuantizedWeight
+
+
+def shard_rows(M: int, world: int) -> tuple[int, list[tuple[int, int]]]:
+    """Padded shard height Mp and the [r0, r1) row range of every rank."""
+    if world < 1:
+        raise ValueError("world size must be positive")
+    mp = (M + world - 1) // world
+    ranges = [(min(r * mp, M), min((r + 1) * mp, M)) for r in range(world)]
+    return mp, ranges
+
+
+def shard_weight(qw: QuantizedWeight, rank: int, world: int) -> QuantizedWeight:
+    """Rows of ``qw`` owned by ``rank``, padded to the common shard height with
+    zero codes (their outputs are discarded after the gather)."""
+    mp, ranges = shard_rows(qw.out_features, world)
+    r0, r1 = ranges[rank]
+    rows = r1 - r0
+
+    def take(t: torch.Tensor) -> torch.Tensor:
+        part = t[r0:r1]
+        if rows == mp:
+            return part.contiguous()
+        pad = torch.zeros((mp - rows,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        if t.dtype.is_floating_point and t is qw.scales:
+            pad.fill_(1.0)
+        return torch.cat((part, pad), dim=0).contiguous()
+
+    per_row = int(qw.scales.shape[0]) == qw.out_features and qw.out_features > 1
+    return QuantizedWeight(
+        codes=take(qw.codes),
+        scales=take(qw.scales) if per_row else qw.scales.contiguous(),
+        zeros=take(qw.zeros) if per_row else qw.zeros.contiguous(),
+        bits=qw.bits,
+        group_size=qw.group_size,
+        in_features=qw.in_features,
+        out_features=mp,
+        symmetric=qw.symmetric,
+        packed=qw.packed,
+        granularity=qw.granularity,
+        channel_scale=qw.channel_scale,
+    )
+
+
+def gather_shards(y_local: torch.Tensor, out: torch.Tensor, group: dist.ProcessGroup | None = None) -> None:
+    """All-gather every rank's [B, Mp] shard into ``out`` [world, B, Mp]."""
+    dist.all_gather_into_tensor(out.view(-1), y_local.contiguous().view(-1), group=group)
+
+
+class RowParallelDequantLinear:
+    """One rank's part of a row-sharded quantized linear layer (no bias)."""
+
+    def __init__(self, shard: QuantizedWeight, out_features: int, rank: int, world: int,
+                 group: dist.ProcessGroup | None = None) -> None:
+        mp, _ = shard_rows(out_features, world)
+        if shard.out_features != mp:
+            raise ValueError("shard height does not match the row split")
+        if shard.codes.device.type != "cuda":
+            raise ValueError("the shard must live on a CUDA device")
+        self.shard = shard
+        self.out_features = out_features
+        self.rank = rank
+        self.world = world
+        self.group = group
+        self.mp = mp
+        self._bufs: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+
+    def _buffers(self, batch: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        if batch not in self._bufs:
+            dev = self.shard.codes.device
+            local = torch.empty((batch, self.mp), dtype=torch.float32, device=dev)
+            gathered = torch.empty((self.world, batch, self.mp), dtype=torch.float32, device=dev)
+            full = torch.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
+            self._bufs[batch] = (local, gathered, full)
+        return self._bufs[batch]
+
+    def forward_local(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's [B, Mp] shard of y."""
+        s = self.shard
+        return _kernels.dequant_gemm(x, s.codes, s.scales, s.zeros, s.channel_scale, s.group_size, s.bits, out=out)
+
+    def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        """y [B, M] on every rank (gather=True), else this rank's [B, Mp] shard."""
+        batch = int(x.shape[0])
+        local, gathered, full = self._buffers(batch)
+        self.forward_local(x, out=local)
+        if not gather:
+            return local
+        if self.world == 1:
+            return local[:, : self.out_features]
+        gather_shards(local, gathered, self.group)
+        _kernels.gather_permute(gathered, self.world, out=full)
+        return full[:, : self.out_features]
