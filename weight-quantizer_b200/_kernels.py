@@ -35,6 +35,7 @@ _sz = ctypes.c_size_t
 SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_status_string": (ctypes.c_char_p, [_int]),
     "wq_last_cuda_error": (ctypes.c_char_p, []),
+    "wq_fault_status": (_int, [_int, ctypes.POINTER(ctypes.c_uint32)]),
     "wq_kernel_info": (_int, [_int, _vp]),
     "wq_dequant_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
     "wq_dequant_gemm_f32": (
@@ -122,6 +123,14 @@ def _cuda_device(tensors: list[torch.Tensor]) -> torch.device:
         if t.device != dev:
             raise ValueError("dequant kernel inputs must be on one CUDA device")
     return dev
+
+
+def fault_status(reset: bool = True) -> int:
+    """The current device's fault word (nonzero: a bounded pipeline wait
+    expired in some launch since the last reset). Synchronizes the device."""
+    v = ctypes.c_uint32(0)
+    _check(library().wq_fault_status(int(reset), ctypes.byref(v)))
+    return int(v.value)
 
 
 def kernel_info(device: int | None = None) -> dict[str, Any]:

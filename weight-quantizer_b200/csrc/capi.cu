@@ -25,6 +25,23 @@ int sm_count() {
     return cached[dev];
 }
 
+// Fault word of this library on every device that loads it.
+__device__ unsigned int g_wq_fault = 0;
+
+unsigned int* fault_word() {
+    static unsigned int* cached[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == nullptr) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_wq_fault) != cudaSuccess) return nullptr;
+        cached[dev] = static_cast<unsigned int*>(ptr);
+    }
+    return cached[dev];
+}
+
 }  // namespace wq
 
 namespace {
@@ -84,6 +101,20 @@ int wq_kernel_info(int device, wq_kernel_info_t* out) {
     out->device_cc = prop.major * 10 + prop.minor;
     out->sm_count = prop.multiProcessorCount;
     std::snprintf(out->device_name, sizeof(out->device_name), "%s", prop.name);
+    return WQ_OK;
+}
+
+int wq_fault_status(int reset, uint32_t* out) {
+    if (out == nullptr) return WQ_E_NULL;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, wq::g_wq_fault, sizeof(v));
+    if (e != cudaSuccess) return cuda_fail(e);
+    *out = v;
+    if (reset && v != 0) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(wq::g_wq_fault, &zero, sizeof(zero));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
     return WQ_OK;
 }
 

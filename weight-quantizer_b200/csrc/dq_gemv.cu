@@ -8,18 +8,28 @@
 //
 //     y[b,m] = sum_chunks scale[m,g] * ( sum_k q[m,k]*x'[b,k]  -  zero[m,g] * sum_k x'[b,k] )
 //
-// with x' = x * channel and a chunk = the codes of one 16-byte load (32 int4 or
+// with x' = x * channel and a chunk = the codes of 16 bytes of a row (32 int4 or
 // 16 int8 codes, always inside one group).
 //
 // Mapping ("activation-stationary"). A row slot of WPR warps covers the whole
 // K extent of a row: lane l of warp w owns chunks c = (w*32 + l) + j*WPR*32,
 // j < NCPL, and keeps x' for those chunks in registers for the entire launch.
-// Rows then stream past: every iteration a slot loads R rows' 16-byte chunks
-// (fully coalesced: a warp reads 512 contiguous bytes per row), multiplies
-// them against its register-resident x', reduces over lanes with shuffles and
-// over the slot's warps through shared memory in a fixed order. CTAs are
-// persistent; x is read from L2 once per slot. There is no workspace and no
-// atomics: the output is deterministic.
+// Rows stream past: every iteration a slot takes R consecutive rows, each lane
+// multiplies its chunks against its register-resident x', and the row sums are
+// reduced over lanes with shuffles and over the slot's warps through shared
+// memory, in a fixed order (deterministic, no atomics, no workspace). CTAs are
+// persistent, so x is read from L2 once per slot.
+//
+// Weight stream. One elected thread per slot moves the R rows of codes (and,
+// for per-row tables whose row length is a multiple of 16 bytes, their scales
+// and zeros) into an NS-deep ring of shared-memory stages with bulk
+// asynchronous copies (cp.async.bulk, the TMA unit's linear mode), completing
+// on one mbarrier per stage. Lanes then read their 16-byte chunk with one
+// shared load: no per-lane address arithmetic or copy instructions. The
+// slot barrier that ends every iteration (for the cross-warp reduction) also
+// tells the producer that the stage it is about to refill has been consumed.
+// Every mbarrier wait is bounded; on expiry the kernel records a fault in the
+// library's fault word and runs to completion without waiting again.
 //
 // Code -> fp32 without conversion instructions. For a 32-bit word of packed
 // codes, masking one code in place (w & 0xF << 4p for int4, w & 0xFF << 8p for
@@ -68,31 +78,31 @@ __device__ __forceinline__ int code_shift(int i) {
     }
 }
 
-template <int BITS, int NB>
-__device__ __forceinline__ void accumulate_word(uint32_t w, const float* xw /* [NB][PER_WORD] */,
+// One 32-bit word of codes against its activations, held as float2 register
+// pairs (the operand form of the packed FMA).
+template <int BITS, int NB, int NCPL, int CH2>
+__device__ __forceinline__ void accumulate_word(uint32_t w, const float2 (&x2)[NCPL][NB][CH2], int j, int base,
                                                 float2 (&acc)[NB]) {
     if (BITS == 4) {
-        const uint32_t t = w >> 24;
+        const uint32_t t = __umulhi(w, 256u);  // w >> 24 on the FMA pipe
         const float2 f01 = make_float2(__uint_as_float(w & 0x0000000Fu), __uint_as_float(w & 0x000000F0u));
         const float2 f23 = make_float2(__uint_as_float(w & 0x00000F00u), __uint_as_float(w & 0x0000F000u));
         const float2 f45 = make_float2(__uint_as_float(w & 0x000F0000u), __uint_as_float(w & 0x00F00000u));
         const float2 f67 = make_float2(__uint_as_float(t & 0x0000000Fu), __uint_as_float(t & 0x000000F0u));
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            const float* xb = xw + b * 8;
-            acc[b] = __ffma2_rn(f01, make_float2(xb[0], xb[1]), acc[b]);
-            acc[b] = __ffma2_rn(f23, make_float2(xb[2], xb[3]), acc[b]);
-            acc[b] = __ffma2_rn(f45, make_float2(xb[4], xb[5]), acc[b]);
-            acc[b] = __ffma2_rn(f67, make_float2(xb[6], xb[7]), acc[b]);
+            acc[b] = __ffma2_rn(f01, x2[j][b][base + 0], acc[b]);
+            acc[b] = __ffma2_rn(f23, x2[j][b][base + 1], acc[b]);
+            acc[b] = __ffma2_rn(f45, x2[j][b][base + 2], acc[b]);
+            acc[b] = __ffma2_rn(f67, x2[j][b][base + 3], acc[b]);
         }
     } else {
         const float2 f01 = make_float2(__uint_as_float(w & 0x000000FFu), __uint_as_float(w & 0x0000FF00u));
-        const float2 f23 = make_float2(__uint_as_float(w & 0x00FF0000u), __uint_as_float(w >> 24));
+        const float2 f23 = make_float2(__uint_as_float(w & 0x00FF0000u), __uint_as_float(__umulhi(w, 256u)));
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            const float* xb = xw + b * 4;
-            acc[b] = __ffma2_rn(f01, make_float2(xb[0], xb[1]), acc[b]);
-            acc[b] = __ffma2_rn(f23, make_float2(xb[2], xb[3]), acc[b]);
+            acc[b] = __ffma2_rn(f01, x2[j][b][base + 0], acc[b]);
+            acc[b] = __ffma2_rn(f23, x2[j][b][base + 1], acc[b]);
         }
     }
 }
@@ -104,29 +114,47 @@ struct GemvParams {
     const float* zeros;
     const float* channel;
     float* y;
+    unsigned int* fault;
     int M, K, NCH;
     int64_t q_stride, ldy;
     int scale_rows, groups, group_size;
-    int wpr;        // warps per row slot
-    int slots;      // row slots per CTA
-    int x_vec4;     // x rows and channel are 16-byte aligned and K % 4 == 0
+    int wpr;          // warps per row slot
+    int slots;        // row slots per CTA
+    int ns;           // pipeline stages per slot
+    int x_vec4;       // x rows and channel are 16-byte aligned and K % 4 == 0
+    int bulk_tables;  // per-row scale/zero tables travel with the codes
+    uint32_t stage_bytes;  // bytes of one stage (128-byte multiple)
 };
 
-constexpr int kMaxSlots = 8;  // named barriers 1..8 (CTA <= 256 threads)
+constexpr int kMaxSlots = 8;   // named barriers 1..8 (CTA <= 256 threads)
+constexpr int kMaxStages = 8;
 
 template <int BITS, int NB, int NCPL, int R>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     constexpr int CH = Fmt<BITS>::CH;
     constexpr int PW = Fmt<BITS>::PER_WORD;
-    extern __shared__ float smem[];
-    // smem: red[2][slots][wpr][R*NB] partials, then emax[slots][wpr][NB]
+    // dynamic smem: stages[slots][ns] (stage_bytes each: codes R*q_stride, then
+    // scales R*groups and zeros R*groups fp32 when bulk_tables), then
+    // mbarriers[slots][ns] (8 B), red[2][slots][wpr][VPAD], emax[slots][wpr][NB]
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int slot = warp / p.wpr;
     const int wslot = warp - slot * p.wpr;
     const int slot_threads = p.wpr * 32;
-    float* red = smem;
-    float* emax = smem + 2 * p.slots * p.wpr * R * NB;
+    const int bar_id = slot + 1;
+    const bool producer = (wslot == 0 && lane == 0);
+    unsigned char* stage_base = smem_raw + (size_t)slot * p.ns * p.stage_bytes;
+    uint64_t* mbar_all = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.slots * p.ns * p.stage_bytes);
+    uint64_t* mbar = mbar_all + slot * p.ns;
+    float* red = reinterpret_cast<float*>(mbar_all + p.slots * p.ns);
+    constexpr int VPAD = (R * NB) <= 1 ? 1 : ((R * NB) <= 2 ? 2 : ((R * NB) <= 4 ? 4 : 8));
+    float* emax = red + 2 * p.slots * p.wpr * VPAD;
+
+    if (producer) {
+        for (int s = 0; s < p.ns; ++s) mbar_init(smem_addr(mbar + s), 1);
+        fence_mbarrier_init();
+    }
 
     // ---- stage x' = x * channel for this lane's chunks in registers ----------
     float xr[NCPL][NB][CH];
@@ -175,7 +203,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
         if (lane == 0) emax[(slot * p.wpr + wslot) * NB + b] = v;
     }
-    asm volatile("bar.sync %0, %1;" ::"r"(slot + 1), "r"(slot_threads));
+    named_barrier(bar_id, slot_threads);  // also publishes the initialized mbarriers
     int eb[NB];
     float sx[NCPL][NB];
 #pragma unroll
@@ -202,126 +230,156 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
             sx[j][b] = sum;
         }
     }
+    float2 x2[NCPL][NB][CH / 2];
+#pragma unroll
+    for (int j = 0; j < NCPL; ++j)
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int i = 0; i < CH / 2; ++i) x2[j][b][i] = make_float2(xr[j][b][2 * i], xr[j][b][2 * i + 1]);
 
-    // ---- stream rows -----------------------------------------------------------
-    const int64_t total_slots = (int64_t)gridDim.x * p.slots;
-    const int64_t gslot = (int64_t)blockIdx.x * p.slots + slot;
-    const int64_t n_iters_total = ((int64_t)p.M + R - 1) / R;
+    // ---- loop invariants -------------------------------------------------------
     const bool multi = p.groups > 1;
+    int goff[NCPL];
+    uint32_t coff[NCPL];
+    bool cvalid[NCPL];
+    float csc_const[NCPL], czr_const[NCPL];
+#pragma unroll
+    for (int j = 0; j < NCPL; ++j) {
+        cvalid[j] = cidx[j] < p.NCH;
+        coff[j] = (uint32_t)cidx[j] * 16u;
+        goff[j] = (multi && cvalid[j]) ? (cidx[j] * CH) / p.group_size : 0;
+        csc_const[j] = 0.0f;
+        czr_const[j] = 0.0f;
+        if (p.scale_rows == 1 && cvalid[j]) {  // one table shared by all rows
+            csc_const[j] = __ldg(p.scales + goff[j]);
+            czr_const[j] = __ldg(p.zeros + goff[j]);
+        }
+    }
+    const int total_slots = (int)gridDim.x * p.slots;
+    const int gslot = (int)blockIdx.x * p.slots + slot;
+    const int n_iters_total = (p.M + R - 1) / R;
+    const uint32_t qs = (uint32_t)p.q_stride;
+    const uint32_t codes_bytes = (uint32_t)R * qs;
+    const uint32_t table_bytes = (uint32_t)(R * p.groups * 4);
+    const uint32_t stage0 = smem_addr(stage_base);
+    const uint32_t mbar0 = smem_addr(mbar);
 
-    uint4 cur[R][NCPL];
-    float csc[R][NCPL], czr[R][NCPL];
-    auto load = [&](int64_t it, uint4 (&cq)[R][NCPL], float (&sc)[R][NCPL], float (&zr)[R][NCPL]) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int64_t row = it * R + r;
-#pragma unroll
-            for (int j = 0; j < NCPL; ++j) {
-                const int c = cidx[j];
-                if (row < p.M && c < p.NCH) {
-                    cq[r][j] = ld_stream_v4(p.q + row * p.q_stride + (int64_t)c * 16);
-                    const int g = multi ? (c * CH) / p.group_size : 0;
-                    const int64_t srow = p.scale_rows == 1 ? 0 : row;
-                    sc[r][j] = __ldg(p.scales + srow * p.groups + g);
-                    zr[r][j] = __ldg(p.zeros + srow * p.groups + g);
-                } else {
-                    cq[r][j] = make_uint4(0u, 0u, 0u, 0u);
-                    sc[r][j] = 0.0f;
-                    zr[r][j] = 0.0f;
-                }
-            }
+    // producer: bulk-copy iteration `it` into stage `s`
+    auto issue = [&](int it, int s) {
+        if (it >= n_iters_total) return;
+        const int row0 = it * R;
+        const int rows = (p.M - row0) < R ? (p.M - row0) : R;
+        const uint32_t cb = (uint32_t)rows * qs;
+        const uint32_t tb = p.bulk_tables ? (uint32_t)(rows * p.groups * 4) : 0u;
+        const uint32_t bar = mbar0 + 8u * (uint32_t)s;
+        const uint32_t dst = stage0 + (uint32_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(bar, cb + 2u * tb);
+        bulk_copy_g2s(dst, p.q + (int64_t)row0 * p.q_stride, cb, bar);
+        if (p.bulk_tables) {
+            bulk_copy_g2s(dst + codes_bytes, p.scales + (int64_t)row0 * p.groups, tb, bar);
+            bulk_copy_g2s(dst + codes_bytes + table_bytes, p.zeros + (int64_t)row0 * p.groups, tb, bar);
         }
     };
 
-    int64_t it = gslot;
-    if (it < n_iters_total) load(it, cur, csc, czr);
-    int parity = 0;
-    for (; it < n_iters_total; it += total_slots) {
-        uint4 nxt[R][NCPL];
-        float nsc[R][NCPL], nzr[R][NCPL];
-        const int64_t nit = it + total_slots;
-        if (nit < n_iters_total) load(nit, nxt, nsc, nzr);
+    if (producer)
+        for (int s = 0; s < p.ns; ++s) issue(gslot + s * total_slots, s);
 
-        float yacc[R][NB];
+    constexpr int V = R * NB;                         // row sums one iteration produces
+    constexpr int VP = V <= 1 ? 1 : (V <= 2 ? 2 : (V <= 4 ? 4 : 8));
+    bool faulted = false;
+    int parity = 0;
+    int s = 0;
+    uint32_t phase = 0;
+    for (int it = gslot; it < n_iters_total; it += total_slots) {
+        if (!faulted && !mbar_wait_bounded(mbar0 + 8u * (uint32_t)s, phase)) {
+            faulted = true;
+            atomicOr(p.fault, 1u);
+        }
+        const unsigned char* stg = stage_base + (size_t)s * p.stage_bytes;
+        const float* tsc = reinterpret_cast<const float*>(stg + codes_bytes);
+        const float* tzr = reinterpret_cast<const float*>(stg + codes_bytes + table_bytes);
+
+        float yv[VP];
+#pragma unroll
+        for (int v = 0; v < VP; ++v) yv[v] = 0.0f;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-#pragma unroll
-            for (int b = 0; b < NB; ++b) yacc[r][b] = 0.0f;
+            const int row = it * R + r;
 #pragma unroll
             for (int j = 0; j < NCPL; ++j) {
-                float2 acc[NB];
-#pragma unroll
-                for (int b = 0; b < NB; ++b) acc[b] = make_float2(0.0f, 0.0f);
-                const uint32_t words[4] = {cur[r][j].x, cur[r][j].y, cur[r][j].z, cur[r][j].w};
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {
-                    float xw[NB * PW];
-#pragma unroll
-                    for (int b = 0; b < NB; ++b)
-#pragma unroll
-                        for (int i = 0; i < PW; ++i) xw[b * PW + i] = xr[j][b][wi * PW + i];
-                    accumulate_word<BITS, NB>(words[wi], xw, acc);
+                const uint4 cq = *reinterpret_cast<const uint4*>(stg + (uint32_t)r * qs + coff[j]);
+                float sc, zr;
+                if (p.scale_rows == 1) {
+                    sc = csc_const[j];
+                    zr = czr_const[j];
+                } else if (p.bulk_tables) {
+                    sc = tsc[r * p.groups + goff[j]];
+                    zr = tzr[r * p.groups + goff[j]];
+                } else {
+                    const int rr = row < p.M ? row : p.M - 1;
+                    sc = __ldg(p.scales + (int64_t)rr * p.groups + goff[j]);
+                    zr = __ldg(p.zeros + (int64_t)rr * p.groups + goff[j]);
                 }
+                // lanes past the row's last chunk read stale stage bytes (finite
+                // once masked, times x' = 0); their scale and zero are forced to 0
+                if (!cvalid[j]) {
+                    sc = 0.0f;
+                    zr = 0.0f;
+                }
+                // two independent accumulation chains per chunk (words x,z and y,w)
+                float2 acc[NB], acc2[NB];
 #pragma unroll
                 for (int b = 0; b < NB; ++b) {
-                    const float a = acc[b].x + acc[b].y;
-                    const float t = fmaf(-czr[r][j], sx[j][b], a);
-                    yacc[r][b] = fmaf(csc[r][j], t, yacc[r][b]);
+                    acc[b] = make_float2(0.0f, 0.0f);
+                    acc2[b] = make_float2(0.0f, 0.0f);
+                }
+                accumulate_word<BITS, NB, NCPL, CH / 2>(cq.x, x2, j, 0 * (PW / 2), acc);
+                accumulate_word<BITS, NB, NCPL, CH / 2>(cq.y, x2, j, 1 * (PW / 2), acc2);
+                accumulate_word<BITS, NB, NCPL, CH / 2>(cq.z, x2, j, 2 * (PW / 2), acc);
+                accumulate_word<BITS, NB, NCPL, CH / 2>(cq.w, x2, j, 3 * (PW / 2), acc2);
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const float a = (acc[b].x + acc2[b].x) + (acc[b].y + acc2[b].y);
+                    const float t = fmaf(-zr, sx[j][b], a);
+                    yv[r * NB + b] = fmaf(sc, t, yv[r * NB + b]);
                 }
             }
         }
-        // reduce over lanes, then over the slot's warps in a fixed order
+
+        // lanes -> one row sum per representative lane (reduce-scatter), then
+        // the slot's warps in a fixed order
+        int idx = 0;
+        const float z = warp_reduce_scatter<VP>(yv, lane, idx);
+        float* rb = red + ((parity * p.slots + slot) * p.wpr) * VP;
+        if ((lane & (32 / VP - 1)) == 0) rb[wslot * VP + idx] = z;
+        // every thread of the slot is done with stage s past this barrier
+        named_barrier(bar_id, slot_threads);
+        if (producer && !faulted) issue(it + p.ns * total_slots, s);
+        if (wslot == 0 && lane < V) {
+            const int r = lane / NB, b = lane - (lane / NB) * NB;
+            const int row = it * R + r;
+            float v = 0.0f;
+            for (int w = 0; w < p.wpr; ++w) v += rb[w * VP + lane];
+            if (row < p.M) {
+                int e = 0;
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int b = 0; b < NB; ++b) yacc[r][b] = warp_sum(yacc[r][b]);
-        if (p.wpr == 1) {
-            if (lane == 0) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int64_t row = it * R + r;
-                    if (row < p.M) {
-#pragma unroll
-                        for (int b = 0; b < NB; ++b) {
-                            const int h = 25 + eb[b], h1 = h / 2;
-                            p.y[(int64_t)b * p.ldy + row] = (yacc[r][b] * pow2i(h1)) * pow2i(h - h1);
-                        }
-                    }
-                }
+                for (int bb = 0; bb < NB; ++bb)
+                    if (bb == b) e = eb[bb];
+                const int h = 25 + e, h1 = h / 2;
+                p.y[(int64_t)b * p.ldy + row] = (v * pow2i(h1)) * pow2i(h - h1);
             }
-        } else {
-            float* rb = red + ((parity * p.slots + slot) * p.wpr) * R * NB;
-            if (lane == 0) {
-#pragma unroll
-                for (int r = 0; r < R; ++r)
-#pragma unroll
-                    for (int b = 0; b < NB; ++b) rb[wslot * R * NB + r * NB + b] = yacc[r][b];
-            }
-            asm volatile("bar.sync %0, %1;" ::"r"(slot + 1), "r"(slot_threads));
-            if (wslot == 0 && lane < R * NB) {
-                const int r = lane / NB, b = lane - (lane / NB) * NB;
-                const int64_t row = it * R + r;
-                float v = 0.0f;
-                for (int w = 0; w < p.wpr; ++w) v += rb[w * R * NB + lane];
-                if (row < p.M) {
-                    int e = 0;
-#pragma unroll
-                    for (int bb = 0; bb < NB; ++bb)
-                        if (bb == b) e = eb[bb];
-                    const int h = 25 + e, h1 = h / 2;
-                    p.y[(int64_t)b * p.ldy + row] = (v * pow2i(h1)) * pow2i(h - h1);
-                }
-            }
-            parity ^= 1;
         }
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int j = 0; j < NCPL; ++j) {
-                cur[r][j] = nxt[r][j];
-                csc[r][j] = nsc[r][j];
-                czr[r][j] = nzr[r][j];
-            }
+        parity ^= 1;
+        if (++s == p.ns) {
+            s = 0;
+            phase ^= 1u;
+        }
+    }
+    // A fault stopped the refills; copies issued before it may still be in
+    // flight into this CTA's shared memory: wait for them (bounded) before exit.
+    if (producer && faulted) {
+        for (int t = 0; t < p.ns; ++t) mbar_wait_bounded(mbar0 + 8u * (uint32_t)t, 0u);
     }
 }
 
@@ -340,7 +398,7 @@ bool choose(int NB, int NCH, Choice& c) {
         const int wpr = (NCH + 32 * ncpl - 1) / (32 * ncpl);
         if (wpr > 8) continue;
         const int waste = wpr * 32 * ncpl - NCH;
-        if (waste < best_waste || (waste == best_waste && ncpl > c.ncpl)) {
+        if (waste < best_waste) {
             best_waste = waste;
             c.ncpl = ncpl;
             c.wpr = wpr;
@@ -355,15 +413,41 @@ bool choose(int NB, int NCH, Choice& c) {
     return true;
 }
 
+// Shared memory of one SM available to resident CTAs (B200: 228 KB, less a
+// 1 KB per-CTA reservation), and the most stages worth keeping in flight.
+constexpr size_t kSmemPerSm = 227 * 1024;
+
 template <int BITS, int NB, int NCPL, int R>
-cudaError_t launch_t(const GemvParams& p, cudaStream_t s) {
+cudaError_t launch_t(GemvParams p, cudaStream_t s) {
     auto kern = gemv_kernel<BITS, NB, NCPL, R>;
     const int threads = p.wpr * p.slots * 32;
-    const size_t smem = sizeof(float) * (size_t)(2 * p.slots * p.wpr * R * NB + p.slots * p.wpr * NB);
-    int occ = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+    const size_t codes_b = (size_t)R * p.q_stride;
+    const size_t table_b = p.bulk_tables ? (size_t)R * p.groups * 4 : 0;
+    p.stage_bytes = (uint32_t)(((codes_b + 2 * table_b) + 127) / 128 * 128);
+    const size_t tail = sizeof(float) * (size_t)(2 * p.slots * p.wpr * 8 + p.slots * p.wpr * NB);
+    // stages: as many as fit while keeping every CTA the registers allow resident
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, kern);
     if (e != cudaSuccess) return e;
-    if (occ < 1) occ = 1;
+    int occ_regs = attr.numRegs > 0 ? 65536 / (attr.numRegs * threads) : 1;
+    if (occ_regs < 1) occ_regs = 1;
+    if (occ_regs > 4) occ_regs = 4;
+    int ns = 0;
+    for (int want = occ_regs; want >= 1 && ns < 3; --want) {
+        const size_t per_cta = kSmemPerSm / want - 1024;
+        ns = (int)((per_cta - tail) / ((size_t)p.slots * (p.stage_bytes + 8)));
+    }
+    if (ns > kMaxStages) ns = kMaxStages;
+    if (ns < 2) ns = 2;
+    p.ns = ns;
+    const size_t smem = (size_t)p.slots * ns * p.stage_bytes + 8 * (size_t)p.slots * ns + tail;
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
     const int64_t iters = ((int64_t)p.M + R - 1) / R;
     int64_t grid = (int64_t)sm_count() * occ;
     const int64_t need = (iters + p.slots - 1) / p.slots;
@@ -377,15 +461,15 @@ template <int BITS>
 cudaError_t dispatch(const GemvParams& p, int NB, int ncpl, cudaStream_t s) {
     switch (NB) {
         case 1: return ncpl == 2 ? launch_t<BITS, 1, 2, 2>(p, s) : launch_t<BITS, 1, 1, 4>(p, s);
-        case 2: return ncpl == 2 ? launch_t<BITS, 2, 2, 2>(p, s) : launch_t<BITS, 2, 1, 2>(p, s);
+        case 2: return ncpl == 2 ? launch_t<BITS, 2, 2, 2>(p, s) : launch_t<BITS, 2, 1, 4>(p, s);
         case 3:
             if constexpr (BITS == 8) {
-                if (ncpl == 2) return launch_t<BITS, 3, 2, 1>(p, s);
+                if (ncpl == 2) return launch_t<BITS, 3, 2, 2>(p, s);
             }
             return launch_t<BITS, 3, 1, 2>(p, s);
         default:
             if constexpr (BITS == 8) {
-                if (ncpl == 2) return launch_t<BITS, 4, 2, 1>(p, s);
+                if (ncpl == 2) return launch_t<BITS, 4, 2, 2>(p, s);
             }
             return launch_t<BITS, 4, 1, 2>(p, s);
     }
@@ -403,6 +487,8 @@ bool gemv_supported(const GemmProblem& p) {
     const int64_t nch = p.q_stride / 16;
     if (nch > (int64_t)8 * 32 * 2) return false;
     if (p.M > ((int64_t)1 << 31) - 64) return false;
+    // a stage holds R (<= 4) rows of codes and tables and must fit twice
+    if (4 * (p.q_stride + 8 * (int64_t)p.groups) > 48 * 1024) return false;
     Choice c{0, 0, 0};
     const int NB = (int)p.B;
     return p.bits == 4 ? choose<4>(NB, (int)nch, c) : choose<8>(NB, (int)nch, c);
@@ -416,6 +502,8 @@ cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t 
     p.zeros = g.zeros;
     p.channel = g.channel;
     p.y = g.y;
+    p.fault = fault_word();
+    if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;
     p.M = (int)g.M;
     p.K = (int)g.K;
     p.NCH = (int)(g.q_stride / 16);
@@ -426,6 +514,12 @@ cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t 
     p.group_size = g.group_size;
     p.x_vec4 = (g.K % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.x) & 15) == 0) &&
                (g.channel == nullptr || (reinterpret_cast<uintptr_t>(g.channel) & 15) == 0);
+    // per-row tables whose rows are whole 16-byte multiples ride with the codes
+    p.bulk_tables = (g.scale_rows != 1) && (g.groups % 4 == 0) &&
+                    ((reinterpret_cast<uintptr_t>(g.scales) & 15) == 0) &&
+                    ((reinterpret_cast<uintptr_t>(g.zeros) & 15) == 0);
+    p.ns = 2;
+    p.stage_bytes = 0;
     Choice c{0, 0, 0};
     const int NB = (int)g.B;
     const bool ok = g.bits == 4 ? choose<4>(NB, p.NCH, c) : choose<8>(NB, p.NCH, c);

@@ -65,4 +65,9 @@ cudaError_t launch_gather_permute(const float* src, int64_t P, int64_t B, int64_
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Device address (current device) of the library's fault word: kernels OR in
+// a bit when a bounded wait expires (1: a pipeline mbarrier wait). nullptr if
+// the symbol cannot be resolved.
+unsigned int* fault_word();
+
 }  // namespace wq
