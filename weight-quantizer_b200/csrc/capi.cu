@@ -94,7 +94,7 @@ int wq_kernel_info(int device, wq_kernel_info_t* out) {
     out->abi_version = WQ_ABI_VERSION;
     out->compiled_sm = 100;
     out->device = device;
-    out->tcgen05 = 0;
+    out->tcgen05 = 1;
     cudaDeviceProp prop;
     cudaError_t e = cudaGetDeviceProperties(&prop, device);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -120,9 +120,10 @@ int wq_fault_status(int reset, uint32_t* out) {
 
 size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
     (void)M;
-    (void)group_size;
-    if (B <= 0 || K <= 0 || (bits != 4 && bits != 8)) return 0;
+    if (B <= 0 || K <= 0 || group_size <= 0 || (bits != 4 && bits != 8)) return 0;
     if (B <= wq::kGemvMaxBatch) return wq::gemv_workspace_bytes(B, K, bits);
+    const bool single_group = group_size >= K;
+    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, K);
     return 0;
 }
 
@@ -180,6 +181,11 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
         const size_t need = wq::gemv_workspace_bytes(B, K, bits);
         if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
         e = wq::launch_gemv(p, workspace, s);
+    } else if (wq::tc_supported(p)) {
+        const size_t need = wq::tc_workspace_bytes(B, K);
+        if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
+        e = wq::launch_tc(p, workspace, s);
     } else {
         e = wq::launch_gemm_simt(p, s);
     }

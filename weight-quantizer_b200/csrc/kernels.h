@@ -30,6 +30,13 @@ size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
 bool gemv_supported(const GemmProblem& p);
 cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
 
+// --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
+// Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
+// single group). Workspace: the fp16 hi/lo planes of x' and 1/S_b.
+bool tc_supported(const GemmProblem& p);
+size_t tc_workspace_bytes(int64_t B, int64_t K);
+cudaError_t launch_tc(const GemmProblem& p, void* workspace, cudaStream_t s);
+
 // --- generic tiled SIMT kernel: any shape, reference per-element formula ---
 cudaError_t launch_gemm_simt(const GemmProblem& p, cudaStream_t s);
 
