@@ -66,7 +66,8 @@ enum wq_status {
     WQ_E_PRE_SCALE_VAL = 17, /* "pre_scale must be finite and positive" (quant.py:247-248) */
     WQ_E_INT4_RANGE = 18,    /* "int4 codes must lie in [0, 15]" (pack.py:22-26) */
     WQ_E_GROUP_MODE = 19,    /* "group_size must be None, 0, or positive" (quant.py:75-76) */
-    WQ_E_LD = 20             /* output row stride smaller than the row length */
+    WQ_E_LD = 20,            /* output row stride smaller than the row length */
+    WQ_E_NOALLOC_LIMIT = 21  /* problem needs more scratch than wq_dequant_gemm_f32_noalloc holds */
 };
 
 /* Message for a status code (static storage; never NULL). */
@@ -116,6 +117,31 @@ WQ_API int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
                         float* y, int64_t ldy,
                         void* workspace, size_t workspace_bytes,
                         void* stream);
+
+/* Same computation as wq_dequant_gemm_f32, for callers that cannot allocate
+ * device memory where they run the layer (a server that reserves all device
+ * memory at start-up and forbids allocation on its request path, or a runtime
+ * that only holds the buffers its caller gives it). No counterpart in the
+ * reference, whose CPU kernel allocates its output itself.
+ *
+ * Instead of a caller-provided workspace it uses one static scratch array of
+ * 32 MiB (33554432 bytes) inside the library; every GPU that
+ * loads the library holds that array until the process exits. It allocates
+ * nothing. A problem whose wq_dequant_gemm_workspace_bytes() exceeds the array
+ * returns WQ_E_NOALLOC_LIMIT (about 4 * B * K bytes are needed on the
+ * tensor-core path: for K = 8192, up to 1023 batch rows). All calls on a
+ * device share the array and every call writes the scratch it reads before
+ * reading it, but calls whose work overlaps on the GPU race on it. The first
+ * call on each device resolves the array's device address
+ * (cudaGetSymbolAddress); make it before capturing a stream. */
+WQ_API int wq_dequant_gemm_f32_noalloc(const float* x, int64_t B, int64_t K,
+                                       const uint8_t* q, int64_t M, int64_t q_cols,
+                                       const float* scales, int64_t scale_rows, int64_t groups,
+                                       const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                                       const float* channel_scale, int64_t channel_len,
+                                       int group_size, int bits,
+                                       float* y, int64_t ldy,
+                                       void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* RTN quantize + pack: replaces `quantize_weight(weight, config,            */

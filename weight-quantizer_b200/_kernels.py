@@ -24,7 +24,7 @@ LIB_PATH = os.path.join(_HERE, "libwq_b200.so")
 
 WQ_OK = 0
 WQ_E_CUDA = 14
-_ARG_ERRORS_AS_VALUEERROR = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15, 16, 17, 18, 19, 20}
+_ARG_ERRORS_AS_VALUEERROR = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15, 16, 17, 18, 19, 20, 21}
 
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         _int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _int, _int, _vp, _vp]
     ),
     "wq_gather_permute_f32": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "wq_dequant_gemm_f32_noalloc": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
+         _int, _int, _vp, _i64, _vp],
+    ),
 }
 
 

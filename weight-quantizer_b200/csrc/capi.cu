@@ -82,6 +82,8 @@ const char* wq_status_string(int status) {
         case WQ_E_INT4_RANGE: return "int4 codes must lie in [0, 15]";
         case WQ_E_GROUP_MODE: return "group_size must be None, 0, or positive";
         case WQ_E_LD: return "output row stride is smaller than the output row length";
+        case WQ_E_NOALLOC_LIMIT:
+            return "problem needs more scratch than the no-allocation entry point holds; use wq_dequant_gemm_f32";
         default: return "unknown status";
     }
 }
