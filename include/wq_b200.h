@@ -75,11 +75,13 @@ WQ_API const char* wq_status_string(int status);
 /* Text of the last CUDA error seen by this library on the calling thread. */
 WQ_API const char* wq_last_cuda_error(void);
 
-/* Fault word of the current device: kernels set bit 0 when a bounded wait on
- * a pipeline barrier expired (the launch then completed without waiting
- * again, and its output is not valid). Synchronizes with the device. `reset`
- * nonzero clears the word after reading it. No counterpart in the reference,
- * whose CPU kernel has no asynchronous waits. */
+/* Fault word of the current device. Bit 0: a bounded wait on a pipeline
+ * barrier expired (the launch then completed without waiting again, and its
+ * output is not valid). Bit 1: the tensor-core path met a zero point that is
+ * not an integer in [0, 1023] (its (code - zero) was rounded to fp16, so that
+ * output is less accurate than the stated tolerance). Synchronizes with the
+ * device. `reset` nonzero clears the word after reading it. No counterpart in
+ * the reference, whose CPU kernel has no asynchronous waits. */
 WQ_API int wq_fault_status(int reset, uint32_t* out);
 
 /* Build/device facts, the counterpart of `_kernels.kernel_info()`

@@ -73,8 +73,9 @@ cudaError_t launch_gather_permute(const float* src, int64_t P, int64_t B, int64_
 int sm_count();
 
 // Device address (current device) of the library's fault word: kernels OR in
-// a bit when a bounded wait expires (1: a pipeline mbarrier wait). nullptr if
-// the symbol cannot be resolved.
+// 1 when a bounded pipeline mbarrier wait expires, 2 when the tensor-core path
+// meets a zero point that is not an integer in [0, 1023]. nullptr if the
+// symbol cannot be resolved.
 unsigned int* fault_word();
 
 }  // namespace wq
