@@ -25,8 +25,8 @@
 // allocates tensor memory and one elected lane issues tcgen05.mma (M = 128,
 // N = BN, K = 16) and tcgen05.commit; warps 2-5 dequantize; warps 6-9 run the
 // epilogue. All hand-offs are mbarriers; every wait is bounded and, on expiry,
-// records bit 0 in the library's fault word and stops waiting. No TMA
-// multicast is used anywhere.
+// records bit 0 in the library's fault word and stops waiting. Every TMA
+// load targets this CTA's own shared memory only.
 //
 // Output tiles are rasterized in bands of 16 batch tiles so the x' planes of a
 // band stay resident in L2 while the weights stream about twice.
