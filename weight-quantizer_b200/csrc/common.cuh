@@ -77,6 +77,12 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// Orders this thread's generic-proxy shared-memory accesses (and those it has
+// observed) before later async-proxy accesses (TMA, bulk copies, tcgen05) to
+// the same shared memory, and the reverse.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

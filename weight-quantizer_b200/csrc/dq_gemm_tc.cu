@@ -4,15 +4,19 @@
 // batched inputs. The contraction runs on the 5th-generation tensor cores with
 // fp32 accuracy from fp16 operands:
 //
-//   * A = (q - zero) for one 128-row weight tile and a 64-wide K tile. Every
-//     code minus an integral zero point is an integer of magnitude <= 255, exact
-//     in fp16. Four dequant warps build A from TMA-loaded packed codes
-//     (int4: LOP3 with the fp16 exponent 0x6400 gives 1024 + code, HSUB2 of
-//     1024 + zero gives the exact difference) and store it in the 128-byte
-//     swizzled K-major layout the MMA reads.
+//   * A = (q - zero) for one 128-row weight tile. Every code minus an integral
+//     zero point is an integer of magnitude <= 255, exact in fp16. Four
+//     dequant warps build A from TMA-loaded packed codes (int4: LOP3 with the
+//     fp16 exponent 0x6400 gives 1024 + code, HSUB2 of 1024 + zero gives the
+//     exact difference) and write it straight into tensor memory with
+//     tcgen05.st (lane = weight row, two fp16 per column), two 64-wide K tiles
+//     per A stage; the MMA reads A from tensor memory.
 //   * B = x' * S_b split into fp16 hi + lo planes by a prep kernel (x' = x *
 //     channel, S_b a per-batch-row power of two putting max|x'_b * S_b| in
-//     [2^13, 2^14)), so hi + lo carries ~22 significant bits of x'.
+//     [2^13, 2^14)), so hi + lo carries ~22 significant bits of x'. The prep
+//     kernel writes the planes already tiled and 128-byte swizzled exactly as
+//     the MMA reads them from shared memory, so one K tile of both planes for
+//     one batch tile is a single contiguous bulk copy.
 //   * D[m, n] = sum_{k in group} A * (hi + lo) accumulates in fp32 in tensor
 //     memory: one accumulator per quantization group, double-buffered, so the
 //     per-row group scale can be applied outside the MMA. Four epilogue warps
@@ -20,13 +24,16 @@
 //     scale[m, g] * D into register accumulators, and at the end write
 //     y[n, m] = acc * 2^-S_b.
 //
-// Roles (one CTA = one 128 x BN output tile): warp 0 issues the TMA loads of
-// the packed codes and the two x' planes into an NS-deep stage ring; warp 1
-// allocates tensor memory and one elected lane issues tcgen05.mma (M = 128,
-// N = BN, K = 16) and tcgen05.commit; warps 2-5 dequantize; warps 6-9 run the
-// epilogue. All hand-offs are mbarriers; every wait is bounded and, on expiry,
-// records bit 0 in the library's fault word and stops waiting. Every TMA
-// load targets this CTA's own shared memory only.
+// Roles (one CTA = one 128 x BN output tile, 11 warps): warp 0 bulk-copies the
+// x' planes into an NS-deep shared-memory ring; warp 10 loads packed codes
+// (several K tiles per 2D TMA box, 128 bytes per row, 128-byte swizzle) into a
+// separate ring that the dequant warps release as soon as they have read it;
+// warp 1 allocates tensor memory and one thread issues tcgen05.mma (M = 128,
+// N = BN, K = 16, A from tensor memory) and tcgen05.commit; warps 2-5
+// dequantize; warps 6-9 run the epilogue. All hand-offs are mbarriers; every
+// wait is bounded and, on expiry, records bit 0 in the library's fault word
+// and stops waiting. Every TMA and bulk load targets this CTA's own shared
+// memory only.
 //
 // Output tiles are rasterized in bands of 16 batch tiles so the x' planes of a
 // band stay resident in L2 while the weights stream about twice.
@@ -43,17 +50,20 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int kThreads = 320;    // 10 warps
+constexpr int kThreads = 352;    // 11 warps
 constexpr int kBand = 16;        // batch tiles per rasterization band
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 6;
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 6, kWarpCodes = 10;
+constexpr int kCodeRowBytes = 128;  // packed code bytes per row per codes stage
+constexpr int kNC = 2;              // codes stages
 
 struct TcParams {
+    const unsigned char* planes;  // tiled x' planes [tiles_n][KT][2][BN][128 B]
     const float* scales;
     const float* zeros;
     const float* inv_s;   // [B] 2^-S_b
     float* y;
     unsigned int* fault;
-    int M, B, KT, groups, ktg, ngroups, scale_rows, bits;
+    int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
     int64_t ldy;
 };
@@ -68,8 +78,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// One lane of the (fully active) warp gets true.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -138,24 +153,59 @@ __device__ __forceinline__ uint4 dq8_int8(uint32_t a, uint32_t b, uint32_t zz) {
                       hsub2_u32(__byte_perm(b, e, 0x4140), zz), hsub2_u32(__byte_perm(b, e, 0x4342), zz));
 }
 
-template <int BN, int NS>
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Tensor memory: 512 columns. Columns [0, 2 BN) hold the two group
+// accumulators; the rest is a ring of A stages, each two K tiles wide
+// (2 x 32 columns of packed fp16 pairs, one row per lane).
+constexpr uint32_t kTmemCols = 512;
+constexpr int kTilesPerA = 2;
+constexpr int kAStageCols = kTilesPerA * BK / 2;
+
+template <int BN, int NS, int BITS>
 struct Smem {
-    static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
-    static constexpr int C_MAX = BM * 64;           // packed codes of one stage (int8 worst case)
-    static constexpr int STAGE = A_BYTES + 2 * B_BYTES + C_MAX;
-    static constexpr int BAR_OFF = NS * STAGE;
-    // barriers: full_b, full_c, full_a, empty per stage; acc_full[2], acc_empty[2]
-    static constexpr int NBAR = 4 * NS + 4;
+    static constexpr int CB = BITS == 4 ? 32 : 64;        // packed code bytes per row per K tile
+    static constexpr int KC = kCodeRowBytes / CB;          // K tiles per codes stage
+    static constexpr int NA = (int)(kTmemCols - 2 * BN) / kAStageCols;   // A stages in tensor memory
+    static constexpr int B_BYTES = BN * 128;               // one plane of one K tile
+    static constexpr int STAGE = 2 * B_BYTES;              // hi + lo planes
+    static constexpr int C_STAGE = BM * kCodeRowBytes;
+    static constexpr int C_OFF = NS * STAGE;
+    static constexpr int BAR_OFF = C_OFF + kNC * C_STAGE;
+    // barriers: full_b, empty_b per B stage; full_a, empty_a per A stage;
+    // c_full, c_empty per codes stage; acc_full[2], acc_empty[2]
+    static constexpr int NBAR = 2 * NS + 2 * NA + 2 * kNC + 4;
     static constexpr int TMEM_SLOT = BAR_OFF + 8 * NBAR;
     static constexpr int TOTAL = TMEM_SLOT + 16;
+    static_assert(STAGE % 1024 == 0 && C_STAGE % 1024 == 0, "tiles must stay 1024-byte aligned for the 128-byte swizzle");
+    static_assert(TOTAL + 1024 <= 227 * 1024, "stage rings exceed the shared memory of one CTA");
+    static_assert(NA >= 2, "tensor memory holds fewer than two A stages");
+    static_assert(KC % kTilesPerA == 0, "a codes stage must hold whole A stages");
 };
 
-template <int BN, int NS>
+template <int BN, int NS, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
-    dq_gemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap map_q,
-                      const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo) {
-    using L = Smem<BN, NS>;
+    dq_gemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap map_q) {
+    using L = Smem<BN, NS, BITS>;
+    constexpr int NA = L::NA;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // the swizzled tiles need 1024-byte alignment of the dynamic window
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,16 +213,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     auto bar = [&](int i) -> uint32_t { return sbase + L::BAR_OFF + 8u * (uint32_t)i; };
     auto full_b = [&](int s) { return bar(s); };
-    auto full_c = [&](int s) { return bar(NS + s); };
+    auto empty_b = [&](int s) { return bar(NS + s); };
     auto full_a = [&](int s) { return bar(2 * NS + s); };
-    auto empty = [&](int s) { return bar(3 * NS + s); };
-    auto acc_full = [&](int b) { return bar(4 * NS + b); };
-    auto acc_empty = [&](int b) { return bar(4 * NS + 2 + b); };
-    auto stage_a = [&](int s) { return sbase + (uint32_t)(s * L::STAGE); };
-    auto stage_bhi = [&](int s) { return sbase + (uint32_t)(s * L::STAGE + L::A_BYTES); };
-    auto stage_blo = [&](int s) { return sbase + (uint32_t)(s * L::STAGE + L::A_BYTES + L::B_BYTES); };
-    auto stage_c = [&](int s) { return sbase + (uint32_t)(s * L::STAGE + L::A_BYTES + 2 * L::B_BYTES); };
-    const int cbytes = p.bits == 4 ? 32 : 64;  // packed codes per row per stage
+    auto empty_a = [&](int s) { return bar(2 * NS + NA + s); };
+    auto c_full = [&](int c) { return bar(2 * NS + 2 * NA + c); };
+    auto c_empty = [&](int c) { return bar(2 * NS + 2 * NA + kNC + c); };
+    auto acc_full = [&](int b) { return bar(2 * NS + 2 * NA + 2 * kNC + b); };
+    auto acc_empty = [&](int b) { return bar(2 * NS + 2 * NA + 2 * kNC + 2 + b); };
+    auto stage_b = [&](int s) { return sbase + (uint32_t)(s * L::STAGE); };
+    auto stage_c = [&](int c) { return sbase + (uint32_t)(L::C_OFF + c * L::C_STAGE); };
 
     // tile coordinates (bands of kBand batch tiles, weight tiles inside a band)
     const int band = blockIdx.x / (p.tiles_m * kBand);
@@ -181,21 +230,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m_tile = inner / bw;
     const int n_tile = band * kBand + (inner - m_tile * bw);
     const int m0 = m_tile * BM, n0 = n_tile * BN;
+    const int n_astages = (p.KT + kTilesPerA - 1) / kTilesPerA;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(full_b(s), 1);
-            mbar_init(full_c(s), 1);
-            mbar_init(full_a(s), 128);
-            mbar_init(empty(s), 1);
+            mbar_init(empty_b(s), 1);
+        }
+        for (int s = 0; s < NA; ++s) {
+            mbar_init(full_a(s), 4);      // one arrival per dequant warp
+            mbar_init(empty_a(s), 1);
+        }
+        for (int c = 0; c < kNC; ++c) {
+            mbar_init(c_full(c), 1);
+            mbar_init(c_empty(c), 4);     // one arrival per dequant warp
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
-            mbar_init(acc_empty(b), 128);
+            mbar_init(acc_empty(b), 4);   // one arrival per epilogue warp
         }
         fence_mbarrier_init();
     }
-    constexpr uint32_t kTmemCols = (2 * BN) < 32 ? 32 : 2 * BN;
     if (warp == kWarpMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + L::TMEM_SLOT),
                      "r"(kTmemCols)
@@ -206,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::TMEM_SLOT);
+    const uint32_t tmem_a0 = tmem + (uint32_t)(2 * BN);
     bool faulted = false;
     auto wait = [&](uint32_t b, uint32_t parity) {
         if (faulted) return;
@@ -214,85 +270,205 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(p.fault, 1u);
         }
     };
+    // warp-wide wait: lane 0 polls the barrier (acquire), __syncwarp then
+    // orders the other lanes after it; the fault flag is shared by the warp
+    auto wait_warp = [&](uint32_t b, uint32_t parity) {
+        if (lane == 0) wait(b, parity);
+        faulted = __shfl_sync(0xffffffffu, faulted ? 1 : 0, 0) != 0;
+        __syncwarp();
+    };
+    // Before the CTA exits, an issuing thread waits (bounded, even after a
+    // fault) for the last phase of every ring slot it filled, so no copy or MMA
+    // that it started is still writing shared or tensor memory. In a
+    // fault-free run these phases have completed already.
+    auto drain = [&](int nslots, int nitems, auto barrier_of) {
+        for (int s = 0; s < nslots && s < nitems; ++s) {
+            const int last_round = (nitems - 1 - s) / nslots;
+            if (!mbar_wait_bounded(barrier_of(s), (uint32_t)(last_round & 1))) atomicOr(p.fault, 1u);
+        }
+    };
 
-    if (warp == kWarpTma) {
+    if (warp == kWarpB) {
+        // x' planes: one bulk copy of both planes of a K tile per stage
         if (lane == 0) {
+            const uint32_t tile_bytes = (uint32_t)L::STAGE;
+            const unsigned char* src = p.planes + (size_t)n_tile * p.KT * tile_bytes;
+            int s = 0;
+            uint32_t ph = 0;
             for (int t = 0; t < p.KT; ++t) {
-                const int s = t % NS, round = t / NS;
-                if (round > 0) wait(empty(s), (uint32_t)((round - 1) & 1));
-                mbar_arrive_expect_tx(full_b(s), 2u * L::B_BYTES);
-                tma_load_2d(stage_bhi(s), &map_hi, t * BK, n0, full_b(s));
-                tma_load_2d(stage_blo(s), &map_lo, t * BK, n0, full_b(s));
-                mbar_arrive_expect_tx(full_c(s), (uint32_t)(BM * cbytes));
-                tma_load_2d(stage_c(s), &map_q, t * cbytes, m0, full_c(s));
+                if (t >= NS) wait(empty_b(s), ph ^ 1u);
+                mbar_arrive_expect_tx(full_b(s), tile_bytes);
+                bulk_copy_g2s(stage_b(s), src, tile_bytes, full_b(s));
+                src += tile_bytes;
+                if (++s == NS) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
+            drain(NS, p.KT, full_b);
+        }
+    } else if (warp == kWarpCodes) {
+        // packed codes: KC K tiles per 2D box (128 rows x 128 bytes, 128-byte
+        // swizzle so that the dequant threads read them without bank conflicts)
+        if (lane == 0) {
+            const int nct = (p.KT + L::KC - 1) / L::KC;
+            int c = 0;
+            uint32_t ph = 0;
+            for (int ct = 0; ct < nct; ++ct) {
+                if (ct >= kNC) wait(c_empty(c), ph ^ 1u);
+                mbar_arrive_expect_tx(c_full(c), (uint32_t)L::C_STAGE);
+                tma_load_2d(stage_c(c), &map_q, ct * kCodeRowBytes, m0, c_full(c));
+                if (++c == kNC) {
+                    c = 0;
+                    ph ^= 1u;
+                }
+            }
+            drain(kNC, nct, c_full);
         }
     } else if (warp == kWarpMma) {
+        // One thread waits and issues. A comes from tensor memory; the B
+        // descriptors are built once and a stage, a plane or a 16-wide K step
+        // only moves the start-address field (address / 16 in bits 0-13).
         if (lane == 0) {
             // kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, N = BN, M = 128
             const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-            for (int t = 0; t < p.KT; ++t) {
-                const int s = t % NS, round = t / NS;
-                const int g = t / p.ktg;
-                const bool first = (t % p.ktg) == 0;
-                const bool last = ((t % p.ktg) == p.ktg - 1) || (t == p.KT - 1);
-                const int buf = g & 1, use = g >> 1;
-                if (first && use > 0) wait(acc_empty(buf), (uint32_t)((use - 1) & 1));
-                wait(full_b(s), (uint32_t)(round & 1));
-                wait(full_a(s), (uint32_t)(round & 1));
+            const uint64_t b_desc0 = sw128_desc(stage_b(0));
+            constexpr uint64_t kStageStep = (uint64_t)(L::STAGE >> 4);
+            constexpr uint64_t kPlaneStep = (uint64_t)(L::B_BYTES >> 4);
+            int sb = 0, sa = 0, gin = 0, g = 0;
+            uint32_t phb = 0, pha = 0;
+            uint64_t b_desc = b_desc0;
+            int t = 0;
+            for (int ja = 0; ja < n_astages; ++ja) {
+                wait(full_a(sa), pha);
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(buf * BN);
+                const uint32_t a_stage = tmem_a0 + (uint32_t)(sa * kAStageCols);
+                for (int h = 0; h < kTilesPerA && t < p.KT; ++h, ++t) {
+                    const bool first = gin == 0;
+                    const bool last = (gin == p.ktg - 1) || (t == p.KT - 1);
+                    const int buf = g & 1, use = g >> 1;
+                    if (first && use > 0) wait(acc_empty(buf), (uint32_t)((use - 1) & 1));
+                    wait(full_b(sb), phb);
+                    tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)(buf * BN);
+                    const uint32_t a_tile = a_stage + (uint32_t)(h * (BK / 2));
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ad = sw128_desc(stage_a(s) + 32u * kk);
-                    mma_f16(d, ad, sw128_desc(stage_bhi(s) + 32u * kk), idesc, (first && kk == 0) ? 0u : 1u);
-                    mma_f16(d, ad, sw128_desc(stage_blo(s) + 32u * kk), idesc, 1u);
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t bd = b_desc + 2u * kk;
+                        mma_f16_ts(d, a_tile + 8u * kk, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                        mma_f16_ts(d, a_tile + 8u * kk, bd + kPlaneStep, idesc, 1u);
+                    }
+                    mma_commit(empty_b(sb));
+                    if (last) {
+                        mma_commit(acc_full(buf));
+                        gin = 0;
+                        ++g;
+                    } else {
+                        ++gin;
+                    }
+                    if (++sb == NS) {
+                        sb = 0;
+                        phb ^= 1u;
+                        b_desc = b_desc0;
+                    } else {
+                        b_desc += kStageStep;
+                    }
                 }
-                mma_commit(empty(s));
-                if (last) mma_commit(acc_full(buf));
+                mma_commit(empty_a(sa));
+                if (++sa == NA) {
+                    sa = 0;
+                    pha ^= 1u;
+                }
             }
+            drain(NS, p.KT, empty_b);
+            drain(NA, n_astages, empty_a);
         }
     } else if (warp < kWarpEpi0) {
-        // ---- dequant: thread r builds row r of A for every stage --------------
-        const int r = threadIdx.x - kWarpDq0 * 32;
+        // ---- dequant: warp w writes TMEM lanes 32 (w % 4) .. + 31, thread =
+        // one weight row; each A stage holds two K tiles ---------------------
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
         const int64_t m = min(m0 + r, p.M - 1);
         const int64_t srow = p.scale_rows == 1 ? 0 : m;
-        const uint32_t a_row = (uint32_t)r * 128u;
         const uint32_t swz = (uint32_t)(r & 7);
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         bool inexact = false;
-        for (int t = 0; t < p.KT; ++t) {
-            const int s = t % NS, round = t / NS;
-            const int g = p.groups == 1 ? 0 : t / p.ktg;
-            const float z = __ldg(p.zeros + srow * p.groups + g);
-            const float zb = 1024.0f + z;
-            const __half zh = __float2half_rn(zb);
-            if (__half2float(zh) != zb || !(z >= 0.0f && z <= 1023.0f)) inexact = true;
-            const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
-            wait(full_c(s), (uint32_t)(round & 1));
-            if (round > 0) wait(empty(s), (uint32_t)((round - 1) & 1));
-            const unsigned char* crow = smem + (s * L::STAGE + L::A_BYTES + 2 * L::B_BYTES) + r * cbytes;
-            unsigned char* arow = smem + s * L::STAGE;
-            if (p.bits == 4) {
-                const uint4 c0 = *reinterpret_cast<const uint4*>(crow);
-                const uint4 c1 = *reinterpret_cast<const uint4*>(crow + 16);
-                const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(arow + a_row + (((uint32_t)c ^ swz) << 4)) = dq8_int4(w[c], zz);
-            } else {
-                uint32_t w[16];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(crow + 16 * i);
-                    w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        // Zero points of groups g + 1 and g + 2 are in flight while group g is
+        // processed (an L2 round trip is longer than one K tile).
+        const float* zrow = p.zeros + srow * p.groups;
+        float z_cur = __ldg(zrow);
+        float z_n1 = p.ngroups > 1 ? __ldg(zrow + 1) : 0.0f;
+        float z_n2 = p.ngroups > 2 ? __ldg(zrow + 2) : 0.0f;
+        int sa = 0, c = 0, kin = 0, gin = 0, g = 0;
+        uint32_t pha = 0, cph = 0;
+        int t = 0;
+        for (int ja = 0; ja < n_astages; ++ja) {
+            if (ja >= NA) wait_warp(empty_a(sa), pha ^ 1u);
+            tc_fence_after();
+            const uint32_t a_stage = tmem_a0 + lane_base + (uint32_t)(sa * kAStageCols);
+            for (int h = 0; h < kTilesPerA && t < p.KT; ++h, ++t) {
+                if (gin == p.ktg) {   // next group: rotate the prefetched zero points
+                    gin = 0;
+                    ++g;
+                    z_cur = z_n1;
+                    z_n1 = z_n2;
+                    if (g + 2 < p.ngroups) z_n2 = __ldg(zrow + g + 2);
                 }
+                const float z = z_cur;
+                const float zb = 1024.0f + z;
+                const __half zh = __float2half_rn(zb);
+                if (__half2float(zh) != zb || !(z >= 0.0f && z <= 1023.0f)) inexact = true;
+                const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
+                if (kin == 0) wait_warp(c_full(c), cph);
+                const unsigned char* crow = smem + L::C_OFF + c * L::C_STAGE + r * kCodeRowBytes;
+                uint32_t a[32];
+                if constexpr (BITS == 4) {
+                    // K tile = 16-byte chunks 2 kin, 2 kin + 1 of the row (swizzled)
+                    const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin) ^ swz) << 4));
+                    const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin + 1) ^ swz) << 4));
+                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(arow + a_row + (((uint32_t)c ^ swz) << 4)) =
-                        dq8_int8(w[2 * c], w[2 * c + 1], zz);
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const uint4 v = dq8_int4(w[cc], zz);
+                        a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
+                    }
+                } else {
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(4 * kin + i) ^ swz) << 4));
+                        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+                    }
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        const uint4 v = dq8_int8(w[2 * cc], w[2 * cc + 1], zz);
+                        a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
+                    }
+                }
+                tmem_st32(a_stage + (uint32_t)(h * (BK / 2)), a);
+                ++gin;
+                if (++kin == L::KC || t == p.KT - 1) {
+                    // every code of this codes stage has been consumed (the
+                    // values reached tcgen05.st); the proxy fence orders the
+                    // reads before the TMA unit refills the stage
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(c_empty(c));
+                    kin = 0;
+                    if (++c == kNC) {
+                        c = 0;
+                        cph ^= 1u;
+                    }
+                }
             }
-            fence_proxy_async_smem();
-            mbar_arrive(full_a(s));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_a(sa));
+            if (++sa == NA) {
+                sa = 0;
+                pha ^= 1u;
+            }
         }
         if (inexact) atomicOr(p.fault, 2u);
     } else {
@@ -304,21 +480,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[BN];
 #pragma unroll
         for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+        // scales of groups g + 1 and g + 2 are in flight while group g is read
+        const float* srow_p = p.scales + srow * p.groups;
+        float sc_n1 = p.ngroups > 1 ? __ldg(srow_p + 1) : 0.0f;
+        float sc_n2 = p.ngroups > 2 ? __ldg(srow_p + 2) : 0.0f;
+        float sc = __ldg(srow_p);
         for (int g = 0; g < p.ngroups; ++g) {
             const int buf = g & 1, use = g >> 1;
-            const float sc = __ldg(p.scales + srow * p.groups + (p.groups == 1 ? 0 : g));
-            wait(acc_full(buf), (uint32_t)(use & 1));
+            wait_warp(acc_full(buf), (uint32_t)(use & 1));
             tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int cc = 0; cc < BN / 32; ++cc) {
                 float v[32];
-                tmem_ld32(taddr + 32u * c, v);
+                tmem_ld32(taddr + 32u * cc, v);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(sc, v[i], acc[c * 32 + i]);
+                for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
             }
             tc_fence_before();
-            mbar_arrive(acc_empty(buf));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(buf));
+            sc = sc_n1;
+            sc_n1 = sc_n2;
+            if (g + 3 < p.ngroups) sc_n2 = __ldg(srow_p + g + 3);
         }
         if (m < p.M) {
 #pragma unroll
@@ -337,17 +521,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// x' = x * channel, S_b from max|x'_b|, hi/lo fp16 planes [B][Kpad], inv_s[b] = 1/S_b.
-__global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float* channel, int B, int K, int Kpad,
-                                                     __half* hi, __half* lo, float* inv_s) {
+// x' = x * channel, S_b from max|x'_b|, fp16 hi/lo planes written in the
+// tiled, swizzled form the kernel copies verbatim: batch tile nt = b / BN,
+// row r = b % BN, K tile kt = k / 64, 16-byte chunk c = (k % 64) / 8 at byte
+// ((nt * KT + kt) * 2 + plane) * BN * 128 + r * 128 + ((c ^ (r & 7)) << 4).
+// Rows b >= B (padding of the last batch tile) are written as zeros.
+__global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float* channel, int B, int K, int KT,
+                                                     int BN, unsigned char* planes, float* inv_s) {
     __shared__ float red[8];
     const int b = blockIdx.x;
-    const float* xb = x + (int64_t)b * K;
+    const bool real = b < B;
+    const float* xb = x + (int64_t)(real ? b : 0) * K;
     float mx = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        float v = xb[k];
-        if (channel != nullptr) v = v * channel[k];
-        mx = fmaxf(mx, fabsf(v));
+    if (real) {
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            float v = xb[k];
+            if (channel != nullptr) v = v * channel[k];
+            mx = fmaxf(mx, fabsf(v));
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -359,19 +550,35 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float
     if (v > 0.0f && v <= 3.4028234e38f) frexpf(v, &e);   // v < 2^e
     e = e < -100 ? -100 : (e > 114 ? 114 : e);
     const float S = pow2i(14 - e);                       // max|x' S| < 2^14
-    if (threadIdx.x == 0) inv_s[b] = pow2i(e - 14);
-    __half* hb = hi + (int64_t)b * Kpad;
-    __half* lb = lo + (int64_t)b * Kpad;
-    for (int k = threadIdx.x; k < Kpad; k += blockDim.x) {
-        float u = 0.0f;
-        if (k < K) {
-            u = xb[k];
-            if (channel != nullptr) u = u * channel[k];
-            u = u * S;
+    if (threadIdx.x == 0 && real) inv_s[b] = pow2i(e - 14);
+    const int nt = b / BN, r = b - nt * BN;
+    const size_t plane_bytes = (size_t)BN * 128;
+    for (int ch = threadIdx.x; ch < KT * 8; ch += blockDim.x) {
+        const int k0 = ch * 8, kt = ch >> 3, c = ch & 7;
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float u[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int k = k0 + 2 * i + j;
+                float t = 0.0f;
+                if (real && k < K) {
+                    t = xb[k];
+                    if (channel != nullptr) t = t * channel[k];
+                    t = t * S;
+                }
+                u[j] = t;
+            }
+            const __half h0 = __float2half_rn(u[0]), h1 = __float2half_rn(u[1]);
+            const __half l0 = __float2half_rn(u[0] - __half2float(h0)), l1 = __float2half_rn(u[1] - __half2float(h1));
+            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         }
-        const __half h = __float2half_rn(u);
-        hb[k] = h;
-        lb[k] = __float2half_rn(u - __half2float(h));
+        unsigned char* tile = planes + ((size_t)nt * KT + kt) * 2 * plane_bytes;
+        const size_t off = (size_t)r * 128 + ((uint32_t)(c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(tile + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(tile + plane_bytes + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
 }
 
@@ -405,38 +612,32 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int64_t kpad_of(int64_t K) { return (K + BK - 1) / BK * BK; }
+int64_t kt_of(int64_t K) { return (K + BK - 1) / BK; }
+int bn_of(int64_t B) { return B <= 32 ? 32 : (B <= 64 ? 64 : 128); }
+int64_t bpad_of(int64_t B) { const int bn = bn_of(B); return (B + bn - 1) / bn * bn; }
 
 struct TcWorkspace {
-    __half* hi;
-    __half* lo;
+    unsigned char* planes;
     float* inv_s;
 };
 
 TcWorkspace carve(void* ws, int64_t B, int64_t K) {
-    const int64_t kp = kpad_of(K);
     unsigned char* p = static_cast<unsigned char*>(ws);
     TcWorkspace w;
-    w.hi = reinterpret_cast<__half*>(p);
-    w.lo = reinterpret_cast<__half*>(p + B * kp * 2);
-    w.inv_s = reinterpret_cast<float*>(p + 2 * B * kp * 2);
+    w.planes = p;
+    w.inv_s = reinterpret_cast<float*>(p + bpad_of(B) * kt_of(K) * BK * 4);
     return w;
 }
 
-template <int BN, int NS>
+template <int BN, int NS, int BITS>
 cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s) {
-    using L = Smem<BN, NS>;
-    const int64_t kp = kpad_of(g.K);
-    CUtensorMap mq, mhi, mlo;
-    const uint32_t cbytes = g.bits == 4 ? 32 : 64;
+    using L = Smem<BN, NS, BITS>;
+    CUtensorMap mq;
     if (!encode_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.q, (uint64_t)g.q_stride, (uint64_t)g.M,
-                   (uint64_t)g.q_stride, cbytes, BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_2d(&mhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.hi, (uint64_t)kp, (uint64_t)g.B, (uint64_t)kp * 2, BK,
-                   BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&mlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.lo, (uint64_t)kp, (uint64_t)g.B, (uint64_t)kp * 2, BK,
-                   BN, CU_TENSOR_MAP_SWIZZLE_128B))
+                   (uint64_t)g.q_stride, kCodeRowBytes, BM, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     TcParams p;
+    p.planes = w.planes;
     p.scales = g.scales;
     p.zeros = g.zeros;
     p.inv_s = w.inv_s;
@@ -445,22 +646,21 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;
     p.M = (int)g.M;
     p.B = (int)g.B;
-    p.KT = (int)(kp / BK);
+    p.KT = (int)kt_of(g.K);
     p.groups = g.groups;
     p.ktg = g.groups == 1 ? p.KT : g.group_size / BK;
     p.ngroups = (p.KT + p.ktg - 1) / p.ktg;
     p.scale_rows = g.scale_rows;
-    p.bits = g.bits;
     p.tiles_m = (int)((g.M + BM - 1) / BM);
     p.tiles_n = (int)((g.B + BN - 1) / BN);
     p.ldy = g.ldy;
     const size_t smem = (size_t)L::TOTAL + 1024;
-    auto kern = dq_gemm_tc_kernel<BN, NS>;
+    auto kern = dq_gemm_tc_kernel<BN, NS, BITS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    kern<<<(unsigned)grid, kThreads, smem, s>>>(p, mq, mhi, mlo);
+    kern<<<(unsigned)grid, kThreads, smem, s>>>(p, mq);
     return cudaGetLastError();
 }
 
@@ -471,23 +671,32 @@ bool tc_supported(const GemmProblem& p) {
     if (p.q_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(p.q) & 15) != 0) return false;
     if (p.groups > 1 && p.group_size % BK != 0) return false;
     if (p.M > 0x7fffff00 || p.B > 0x7fffff00) return false;
-    if (kpad_of(p.K) / BK > 0x7fffffff) return false;
+    if (kt_of(p.K) > 0x7fffffff / 8) return false;
     return encode_fn() != nullptr;
 }
 
 size_t tc_workspace_bytes(int64_t B, int64_t K) {
-    return (size_t)(2 * B * kpad_of(K) * 2 + B * 4 + 256);
+    // fp16 hi + lo planes of the padded batch, then 1/S_b
+    return (size_t)(bpad_of(B) * kt_of(K) * BK * 4 + B * 4 + 256);
 }
 
 cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
     const TcWorkspace w = carve(workspace, g.B, g.K);
-    const int64_t kp = kpad_of(g.K);
-    prep_x_kernel<<<(unsigned)g.B, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kp, w.hi, w.lo, w.inv_s);
+    const int bn = bn_of(g.B);
+    const int64_t bpad = bpad_of(g.B);
+    prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn, w.planes,
+                                                 w.inv_s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (g.B <= 32) return launch_bn<32, 4>(g, w, s);
-    if (g.B <= 64) return launch_bn<64, 4>(g, w, s);
-    return launch_bn<128, 3>(g, w, s);
+    // x' stage counts: 192 KB of planes next to two 16 KB codes stages
+    if (g.bits == 4) {
+        if (bn == 32) return launch_bn<32, 12, 4>(g, w, s);
+        if (bn == 64) return launch_bn<64, 12, 4>(g, w, s);
+        return launch_bn<128, 6, 4>(g, w, s);
+    }
+    if (bn == 32) return launch_bn<32, 12, 8>(g, w, s);
+    if (bn == 64) return launch_bn<64, 12, 8>(g, w, s);
+    return launch_bn<128, 6, 8>(g, w, s);
 }
 
 }  // namespace wq

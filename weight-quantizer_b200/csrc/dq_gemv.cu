@@ -355,7 +355,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         if ((lane & (32 / VP - 1)) == 0) rb[wslot * VP + idx] = z;
         // every thread of the slot is done with stage s past this barrier
         named_barrier(bar_id, slot_threads);
-        if (producer && !faulted) issue(it + p.ns * total_slots, s);
+        if (producer && !faulted) {
+            fence_proxy_async_smem();   // the slot's reads of stage s before the bulk copy refills it
+            issue(it + p.ns * total_slots, s);
+        }
         if (wslot == 0 && lane < V) {
             const int r = lane / NB, b = lane - (lane / NB) * NB;
             const int row = it * R + r;
