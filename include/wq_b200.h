@@ -131,7 +131,7 @@ WQ_API int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
  * loads the library holds that array until the process exits. It allocates
  * nothing. A problem whose wq_dequant_gemm_workspace_bytes() exceeds the array
  * returns WQ_E_NOALLOC_LIMIT (about 4 * B * K bytes are needed on the
- * tensor-core path: for K = 8192, up to 1023 batch rows). All calls on a
+ * tensor-core path: for K = 8192, up to 896 batch rows). All calls on a
  * device share the array and every call writes the scratch it reads before
  * reading it, but calls whose work overlaps on the GPU race on it. The first
  * call on each device resolves the array's device address

@@ -326,58 +326,89 @@ __global__ void __launch_bounds__(kThreads, 1)
             drain(kNC, nct, c_full);
         }
     } else if (warp == kWarpMma) {
-        // One thread waits and issues. A comes from tensor memory; the B
-        // descriptors are built once and a stage, a plane or a 16-wide K step
-        // only moves the start-address field (address / 16 in bits 0-13).
+        // One thread issues every MMA. Any shared-memory or barrier operation
+        // this thread issues waits behind its own queued tcgen05.mma
+        // instructions, so each wait point costs a pipeline drain. The thread
+        // therefore waits (blocking) only for the next tile, then probes the
+        // following tiles without blocking and issues every tile that is
+        // ready, up to kIssueBatch, before it touches a barrier again.
+        // A comes from tensor memory; B descriptors are built once and a
+        // stage, a plane or a 16-wide K step only moves the start-address
+        // field (address / 16 in bits 0-13).
         if (lane == 0) {
+            constexpr int kIssueBatch = 8;
             // kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, N = BN, M = 128
             const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             const uint64_t b_desc0 = sw128_desc(stage_b(0));
-            constexpr uint64_t kStageStep = (uint64_t)(L::STAGE >> 4);
             constexpr uint64_t kPlaneStep = (uint64_t)(L::B_BYTES >> 4);
-            int sb = 0, sa = 0, gin = 0, g = 0;
-            uint32_t phb = 0, pha = 0;
-            uint64_t b_desc = b_desc0;
-            int t = 0;
-            for (int ja = 0; ja < n_astages; ++ja) {
-                wait(full_a(sa), pha);
+            // per-tile pipeline position; advance() moves it to the next tile
+            struct Pos {
+                int t, sb, sa, h, gin, g;
+                uint32_t phb, pha;
+            };
+            auto advance = [&](Pos& x) {
+                const bool last = (x.gin == p.ktg - 1) || (x.t == p.KT - 1);
+                if (last) {
+                    x.gin = 0;
+                    ++x.g;
+                } else {
+                    ++x.gin;
+                }
+                if (++x.sb == NS) {
+                    x.sb = 0;
+                    x.phb ^= 1u;
+                }
+                if (++x.h == kTilesPerA) {
+                    x.h = 0;
+                    if (++x.sa == NA) {
+                        x.sa = 0;
+                        x.pha ^= 1u;
+                    }
+                }
+                ++x.t;
+            };
+            // the barriers tile x needs: its x' stage, its A stage (first
+            // tile of the stage), its accumulator (first tile of a group)
+            auto ready = [&](const Pos& x, bool block) -> bool {
+                const int use = x.g >> 1;
+                if (x.gin == 0 && use > 0) {
+                    const uint32_t b = acc_empty(x.g & 1), par = (uint32_t)((use - 1) & 1);
+                    if (block) wait(b, par); else if (!mbar_test_wait(b, par)) return false;
+                }
+                if (block) wait(full_b(x.sb), x.phb); else if (!mbar_test_wait(full_b(x.sb), x.phb)) return false;
+                if (x.h == 0) {
+                    if (block) wait(full_a(x.sa), x.pha); else if (!mbar_test_wait(full_a(x.sa), x.pha)) return false;
+                }
+                return true;
+            };
+            Pos cur{0, 0, 0, 0, 0, 0, 0u, 0u};
+            while (cur.t < p.KT) {
+                ready(cur, true);
+                int n = 1;
+                Pos probe = cur;
+                advance(probe);
+                while (n < kIssueBatch && probe.t < p.KT && !faulted && ready(probe, false)) {
+                    ++n;
+                    advance(probe);
+                }
                 tc_fence_after();
-                const uint32_t a_stage = tmem_a0 + (uint32_t)(sa * kAStageCols);
-                for (int h = 0; h < kTilesPerA && t < p.KT; ++h, ++t) {
-                    const bool first = gin == 0;
-                    const bool last = (gin == p.ktg - 1) || (t == p.KT - 1);
-                    const int buf = g & 1, use = g >> 1;
-                    if (first && use > 0) wait(acc_empty(buf), (uint32_t)((use - 1) & 1));
-                    wait(full_b(sb), phb);
-                    tc_fence_after();
+                for (int i = 0; i < n; ++i) {
+                    const bool first = cur.gin == 0;
+                    const bool last = (cur.gin == p.ktg - 1) || (cur.t == p.KT - 1);
+                    const int buf = cur.g & 1;
                     const uint32_t d = tmem + (uint32_t)(buf * BN);
-                    const uint32_t a_tile = a_stage + (uint32_t)(h * (BK / 2));
+                    const uint32_t a_tile = tmem_a0 + (uint32_t)(cur.sa * kAStageCols + cur.h * (BK / 2));
+                    const uint64_t b_desc = b_desc0 + (uint64_t)(cur.sb * (L::STAGE >> 4));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t bd = b_desc + 2u * kk;
                         mma_f16_ts(d, a_tile + 8u * kk, bd, idesc, (first && kk == 0) ? 0u : 1u);
                         mma_f16_ts(d, a_tile + 8u * kk, bd + kPlaneStep, idesc, 1u);
                     }
-                    mma_commit(empty_b(sb));
-                    if (last) {
-                        mma_commit(acc_full(buf));
-                        gin = 0;
-                        ++g;
-                    } else {
-                        ++gin;
-                    }
-                    if (++sb == NS) {
-                        sb = 0;
-                        phb ^= 1u;
-                        b_desc = b_desc0;
-                    } else {
-                        b_desc += kStageStep;
-                    }
-                }
-                mma_commit(empty_a(sa));
-                if (++sa == NA) {
-                    sa = 0;
-                    pha ^= 1u;
+                    mma_commit(empty_b(cur.sb));
+                    if (last) mma_commit(acc_full(buf));
+                    if (cur.h == kTilesPerA - 1 || cur.t == p.KT - 1) mma_commit(empty_a(cur.sa));
+                    advance(cur);
                 }
             }
             drain(NS, p.KT, empty_b);

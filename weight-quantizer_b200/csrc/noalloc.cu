@@ -15,7 +15,7 @@
 //     Every GPU that loads this library holds it until the process exits.
 //   - A problem whose workspace query exceeds it is rejected with
 //     WQ_E_NOALLOC_LIMIT (the tensor-core path needs about 4 * B * K bytes, so
-//     for K = 8192 up to 1023 batch rows fit).
+//     for K = 8192 up to 896 batch rows fit).
 //   - All calls on a device share the one array. The tensor-core path writes
 //     every scratch byte it reads before reading it, so nothing has to be
 //     cleared between calls, but two calls whose work overlaps on the GPU
