@@ -136,15 +136,16 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// 8 int4 codes (one 32-bit word, k ascending) -> 8 fp16 values (code - zero),
-// packed as 16 bytes in k order; zz = half2(1024 + zero) twice.
+// 8 int4 codes (one 32-bit word, k ascending) -> 8 fp16 values (code - zero)
+// in the order the nibble masks produce them, k0 k4 k1 k5 k2 k6 k3 k7; the
+// prep kernel stores the x' planes of int4 layers in the same order inside
+// every group of 8, so the products pair up without a byte shuffle.
+// zz = half2(1024 + zero) twice.
 __device__ __forceinline__ uint4 dq8_int4(uint32_t w, uint32_t zz) {
-    const uint32_t t0 = hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), zz);          // k0, k4
-    const uint32_t t1 = hsub2_u32(lop3_and_or(w >> 4, 0x000F000Fu, 0x64006400u), zz);     // k1, k5
-    const uint32_t t2 = hsub2_u32(lop3_and_or(w >> 8, 0x000F000Fu, 0x64006400u), zz);     // k2, k6
-    const uint32_t t3 = hsub2_u32(lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u), zz);    // k3, k7
-    return make_uint4(__byte_perm(t0, t1, 0x5410), __byte_perm(t2, t3, 0x5410), __byte_perm(t0, t1, 0x7632),
-                      __byte_perm(t2, t3, 0x7632));
+    return make_uint4(hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), zz),          // k0, k4
+                      hsub2_u32(lop3_and_or(w >> 4, 0x000F000Fu, 0x64006400u), zz),     // k1, k5
+                      hsub2_u32(lop3_and_or(w >> 8, 0x000F000Fu, 0x64006400u), zz),     // k2, k6
+                      hsub2_u32(lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u), zz));   // k3, k7
 }
 // 8 int8 codes (two words) -> 8 fp16 (code - zero)
 __device__ __forceinline__ uint4 dq8_int8(uint32_t a, uint32_t b, uint32_t zz) {
@@ -556,9 +557,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // tiled, swizzled form the kernel copies verbatim: batch tile nt = b / BN,
 // row r = b % BN, K tile kt = k / 64, 16-byte chunk c = (k % 64) / 8 at byte
 // ((nt * KT + kt) * 2 + plane) * BN * 128 + r * 128 + ((c ^ (r & 7)) << 4).
-// Rows b >= B (padding of the last batch tile) are written as zeros.
+// Rows b >= B (padding of the last batch tile) are written as zeros. For
+// int4 layers (`nibble_order`) the 8 values of a chunk are stored in the order
+// k0 k4 k1 k5 k2 k6 k3 k7, matching the order the dequant warps produce A in.
 __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float* channel, int B, int K, int KT,
-                                                     int BN, unsigned char* planes, float* inv_s) {
+                                                     int BN, bool nibble_order, unsigned char* planes, float* inv_s) {
     __shared__ float red[8];
     const int b = blockIdx.x;
     const bool real = b < B;
@@ -592,7 +595,7 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float
             float u[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int k = k0 + 2 * i + j;
+                const int k = k0 + (nibble_order ? i + 4 * j : 2 * i + j);
                 float t = 0.0f;
                 if (real && k < K) {
                     t = xb[k];
@@ -715,8 +718,8 @@ cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
     const TcWorkspace w = carve(workspace, g.B, g.K);
     const int bn = bn_of(g.B);
     const int64_t bpad = bpad_of(g.B);
-    prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn, w.planes,
-                                                 w.inv_s);
+    prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn,
+                                                 g.bits == 4, w.planes, w.inv_s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // x' stage counts: 192 KB of planes next to two 16 KB codes stages
