@@ -129,13 +129,17 @@ struct GemvParams {
 constexpr int kMaxSlots = 8;   // named barriers 1..8 (CTA <= 256 threads)
 constexpr int kMaxStages = 8;
 
-template <int BITS, int NB, int NCPL, int R>
+// LEAN: per-row scale/zero tables travel with the codes (bulk_tables) and every
+// lane's chunks lie inside the row, so the inner loop carries no table-source
+// or validity selects.
+template <int BITS, int NB, int NCPL, int R, bool LEAN>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     constexpr int CH = Fmt<BITS>::CH;
     constexpr int PW = Fmt<BITS>::PER_WORD;
     // dynamic smem: stages[slots][ns] (stage_bytes each: codes R*q_stride, then
     // scales R*groups and zeros R*groups fp32 when bulk_tables), then
-    // mbarriers[slots][ns] (8 B), red[2][slots][wpr][VPAD], emax[slots][wpr][NB]
+    // full mbarriers[slots][ns], consumed mbarriers[slots][ns] (8 B each),
+    // red[slots][ns][wpr][VPAD], emax[slots][wpr][NB], fills[slots][ns] (u32)
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -147,13 +151,51 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     unsigned char* stage_base = smem_raw + (size_t)slot * p.ns * p.stage_bytes;
     uint64_t* mbar_all = reinterpret_cast<uint64_t*>(smem_raw + (size_t)p.slots * p.ns * p.stage_bytes);
     uint64_t* mbar = mbar_all + slot * p.ns;
-    float* red = reinterpret_cast<float*>(mbar_all + p.slots * p.ns);
+    uint64_t* cbar = mbar_all + p.slots * p.ns + slot * p.ns;
     constexpr int VPAD = (R * NB) <= 1 ? 1 : ((R * NB) <= 2 ? 2 : ((R * NB) <= 4 ? 4 : 8));
-    float* emax = red + 2 * p.slots * p.wpr * VPAD;
+    static_assert(R * NB <= 8, "at most 8 row sums per iteration");
+    float* red = reinterpret_cast<float*>(mbar_all + 2 * p.slots * p.ns) + (size_t)slot * p.ns * p.wpr * VPAD;
+    float* emax = reinterpret_cast<float*>(mbar_all + 2 * p.slots * p.ns) + (size_t)p.slots * p.ns * p.wpr * VPAD;
+    uint32_t* fills = reinterpret_cast<uint32_t*>(emax + p.slots * p.wpr * NB) + slot * p.ns;
 
+    const int total_slots = (int)gridDim.x * p.slots;
+    const int gslot = (int)blockIdx.x * p.slots + slot;
+    const int n_iters_total = (p.M + R - 1) / R;
+    const uint32_t qs = (uint32_t)p.q_stride;
+    const uint32_t codes_bytes = (uint32_t)R * qs;
+    const uint32_t table_bytes = (uint32_t)(R * p.groups * 4);
+    const uint32_t stage0 = smem_addr(stage_base);
+    const uint32_t mbar0 = smem_addr(mbar);
+    const uint32_t cbar0 = smem_addr(cbar);
+
+    // producer: bulk-copy iteration `it` into stage `s`
+    auto issue = [&](int it, int s) {
+        if (it >= n_iters_total) return;
+        const int row0 = it * R;
+        const int rows = (p.M - row0) < R ? (p.M - row0) : R;
+        const uint32_t cb = (uint32_t)rows * qs;
+        const uint32_t tb = p.bulk_tables ? (uint32_t)(rows * p.groups * 4) : 0u;
+        const uint32_t bar = mbar0 + 8u * (uint32_t)s;
+        const uint32_t dst = stage0 + (uint32_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(bar, cb + 2u * tb);
+        bulk_copy_g2s(dst, p.q + (int64_t)row0 * p.q_stride, cb, bar);
+        ++fills[s];   // only the thread issuing for this slot touches it between barriers
+        if (p.bulk_tables) {
+            bulk_copy_g2s(dst + codes_bytes, p.scales + (int64_t)row0 * p.groups, tb, bar);
+            bulk_copy_g2s(dst + codes_bytes + table_bytes, p.zeros + (int64_t)row0 * p.groups, tb, bar);
+        }
+    };
+
+    // The weight stream starts before x' is staged: the first NS stages are in
+    // flight while the slot loads x, finds max|x'| and scales it.
     if (producer) {
-        for (int s = 0; s < p.ns; ++s) mbar_init(smem_addr(mbar + s), 1);
+        for (int s = 0; s < p.ns; ++s) {
+            mbar_init(smem_addr(mbar + s), 1);
+            mbar_init(smem_addr(cbar + s), (uint32_t)p.wpr);   // one arrival per warp of the slot
+            fills[s] = 0;
+        }
         fence_mbarrier_init();
+        for (int s = 0; s < p.ns; ++s) issue(gslot + s * total_slots, s);
     }
 
     // ---- stage x' = x * channel for this lane's chunks in registers ----------
@@ -256,40 +298,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
             czr_const[j] = __ldg(p.zeros + goff[j]);
         }
     }
-    const int total_slots = (int)gridDim.x * p.slots;
-    const int gslot = (int)blockIdx.x * p.slots + slot;
-    const int n_iters_total = (p.M + R - 1) / R;
-    const uint32_t qs = (uint32_t)p.q_stride;
-    const uint32_t codes_bytes = (uint32_t)R * qs;
-    const uint32_t table_bytes = (uint32_t)(R * p.groups * 4);
-    const uint32_t stage0 = smem_addr(stage_base);
-    const uint32_t mbar0 = smem_addr(mbar);
-
-    // producer: bulk-copy iteration `it` into stage `s`
-    auto issue = [&](int it, int s) {
-        if (it >= n_iters_total) return;
-        const int row0 = it * R;
-        const int rows = (p.M - row0) < R ? (p.M - row0) : R;
-        const uint32_t cb = (uint32_t)rows * qs;
-        const uint32_t tb = p.bulk_tables ? (uint32_t)(rows * p.groups * 4) : 0u;
-        const uint32_t bar = mbar0 + 8u * (uint32_t)s;
-        const uint32_t dst = stage0 + (uint32_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(bar, cb + 2u * tb);
-        bulk_copy_g2s(dst, p.q + (int64_t)row0 * p.q_stride, cb, bar);
-        if (p.bulk_tables) {
-            bulk_copy_g2s(dst + codes_bytes, p.scales + (int64_t)row0 * p.groups, tb, bar);
-            bulk_copy_g2s(dst + codes_bytes + table_bytes, p.zeros + (int64_t)row0 * p.groups, tb, bar);
-        }
-    };
-
-    if (producer)
-        for (int s = 0; s < p.ns; ++s) issue(gslot + s * total_slots, s);
 
     constexpr int V = R * NB;                         // row sums one iteration produces
     constexpr int VP = V <= 1 ? 1 : (V <= 2 ? 2 : (V <= 4 ? 4 : 8));
     bool faulted = false;
-    int parity = 0;
-    int s = 0;
+    int s = 0, fin = 0, n_local = 0;
     uint32_t phase = 0;
     for (int it = gslot; it < n_iters_total; it += total_slots) {
         if (!faulted && !mbar_wait_bounded(mbar0 + 8u * (uint32_t)s, phase)) {
@@ -305,25 +318,28 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         for (int v = 0; v < VP; ++v) yv[v] = 0.0f;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            const int row = it * R + r;
 #pragma unroll
             for (int j = 0; j < NCPL; ++j) {
                 const uint4 cq = *reinterpret_cast<const uint4*>(stg + (uint32_t)r * qs + coff[j]);
                 float sc, zr;
-                if (p.scale_rows == 1) {
+                if constexpr (LEAN) {
+                    sc = tsc[r * p.groups + goff[j]];
+                    zr = tzr[r * p.groups + goff[j]];
+                } else if (p.scale_rows == 1) {
                     sc = csc_const[j];
                     zr = czr_const[j];
                 } else if (p.bulk_tables) {
                     sc = tsc[r * p.groups + goff[j]];
                     zr = tzr[r * p.groups + goff[j]];
                 } else {
+                    const int row = it * R + r;
                     const int rr = row < p.M ? row : p.M - 1;
                     sc = __ldg(p.scales + (int64_t)rr * p.groups + goff[j]);
                     zr = __ldg(p.zeros + (int64_t)rr * p.groups + goff[j]);
                 }
                 // lanes past the row's last chunk read stale stage bytes (finite
                 // once masked, times x' = 0); their scale and zero are forced to 0
-                if (!cvalid[j]) {
+                if (!LEAN && !cvalid[j]) {
                     sc = 0.0f;
                     zr = 0.0f;
                 }
@@ -351,38 +367,57 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         // the slot's warps in a fixed order
         int idx = 0;
         const float z = warp_reduce_scatter<VP>(yv, lane, idx);
-        float* rb = red + ((parity * p.slots + slot) * p.wpr) * VP;
-        if ((lane & (32 / VP - 1)) == 0) rb[wslot * VP + idx] = z;
-        // every thread of the slot is done with stage s past this barrier
-        named_barrier(bar_id, slot_threads);
-        if (producer && !faulted) {
-            fence_proxy_async_smem();   // the slot's reads of stage s before the bulk copy refills it
-            issue(it + p.ns * total_slots, s);
-        }
-        if (wslot == 0 && lane < V) {
-            const int r = lane / NB, b = lane - (lane / NB) * NB;
-            const int row = it * R + r;
-            float v = 0.0f;
-            for (int w = 0; w < p.wpr; ++w) v += rb[w * VP + lane];
-            if (row < p.M) {
-                int e = 0;
+        float* rb = red + (size_t)s * p.wpr * VPAD;
+        if ((lane & (32 / VP - 1)) == 0) rb[wslot * VPAD + idx] = z;
+        // This warp is done with stage s and has published its partial sums.
+        // No slot-wide barrier: one warp per iteration (rotating) waits for the
+        // others, finishes the rows and refills the stage; the rest move on.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cbar0 + 8u * (uint32_t)s);
+        if (wslot == fin) {
+            if (lane == 0 && !faulted && !mbar_wait_bounded(cbar0 + 8u * (uint32_t)s, phase)) {
+                faulted = true;
+                atomicOr(p.fault, 1u);
+            }
+            faulted = __shfl_sync(0xffffffffu, faulted ? 1 : 0, 0) != 0;
+            __syncwarp();
+            if (lane < V) {
+                const int r = lane / NB, b = lane - (lane / NB) * NB;
+                const int row = it * R + r;
+                float v = 0.0f;
+                for (int w = 0; w < p.wpr; ++w) v += rb[w * VPAD + lane];
+                if (row < p.M) {
+                    int e = 0;
 #pragma unroll
-                for (int bb = 0; bb < NB; ++bb)
-                    if (bb == b) e = eb[bb];
-                const int h = 25 + e, h1 = h / 2;
-                p.y[(int64_t)b * p.ldy + row] = (v * pow2i(h1)) * pow2i(h - h1);
+                    for (int bb = 0; bb < NB; ++bb)
+                        if (bb == b) e = eb[bb];
+                    const int h = 25 + e, h1 = h / 2;
+                    p.y[(int64_t)b * p.ldy + row] = (v * pow2i(h1)) * pow2i(h - h1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && !faulted) {
+                fence_proxy_async_smem();   // the slot's reads of stage s before the bulk copy refills it
+                issue(it + p.ns * total_slots, s);
             }
         }
-        parity ^= 1;
+        if (++fin == p.wpr) fin = 0;
         if (++s == p.ns) {
             s = 0;
             phase ^= 1u;
         }
+        ++n_local;
     }
-    // A fault stopped the refills; copies issued before it may still be in
-    // flight into this CTA's shared memory: wait for them (bounded) before exit.
-    if (producer && faulted) {
-        for (int t = 0; t < p.ns; ++t) mbar_wait_bounded(mbar0 + 8u * (uint32_t)t, 0u);
+    // Copies issued before a fault may still be in flight into this CTA's
+    // shared memory: once the whole slot is past its loop, the first warp
+    // waits (bounded) for the last fill of every stage. In a fault-free run
+    // those phases have completed already.
+    named_barrier(bar_id, slot_threads);
+    if (wslot == 0 && lane == 0) {
+        for (int t = 0; t < p.ns; ++t) {
+            const uint32_t n = fills[t];
+            if (n > 0 && !mbar_wait_bounded(mbar0 + 8u * (uint32_t)t, (n - 1u) & 1u)) atomicOr(p.fault, 1u);
+        }
     }
 }
 
@@ -420,14 +455,16 @@ bool choose(int NB, int NCH, Choice& c) {
 // 1 KB per-CTA reservation), and the most stages worth keeping in flight.
 constexpr size_t kSmemPerSm = 227 * 1024;
 
-template <int BITS, int NB, int NCPL, int R>
+template <int BITS, int NB, int NCPL, int R, bool LEAN>
 cudaError_t launch_t(GemvParams p, cudaStream_t s) {
-    auto kern = gemv_kernel<BITS, NB, NCPL, R>;
+    auto kern = gemv_kernel<BITS, NB, NCPL, R, LEAN>;
     const int threads = p.wpr * p.slots * 32;
     const size_t codes_b = (size_t)R * p.q_stride;
     const size_t table_b = p.bulk_tables ? (size_t)R * p.groups * 4 : 0;
     p.stage_bytes = (uint32_t)(((codes_b + 2 * table_b) + 127) / 128 * 128);
-    const size_t tail = sizeof(float) * (size_t)(2 * p.slots * p.wpr * 8 + p.slots * p.wpr * NB);
+    // per stage: a consumed mbarrier and the warps' partial sums; then emax
+    const size_t red_b = sizeof(float) * (size_t)p.slots * p.wpr * 8;   // one stage's partial sums
+    const size_t tail = sizeof(float) * (size_t)p.slots * p.wpr * NB + sizeof(uint32_t) * (size_t)p.slots * kMaxStages;
     // stages: as many as fit while keeping every CTA the registers allow resident
     cudaFuncAttributes attr;
     cudaError_t e = cudaFuncGetAttributes(&attr, kern);
@@ -438,12 +475,12 @@ cudaError_t launch_t(GemvParams p, cudaStream_t s) {
     int ns = 0;
     for (int want = occ_regs; want >= 1 && ns < 3; --want) {
         const size_t per_cta = kSmemPerSm / want - 1024;
-        ns = (int)((per_cta - tail) / ((size_t)p.slots * (p.stage_bytes + 8)));
+        ns = (int)((per_cta - tail) / ((size_t)p.slots * (p.stage_bytes + 16) + red_b));
     }
     if (ns > kMaxStages) ns = kMaxStages;
     if (ns < 2) ns = 2;
     p.ns = ns;
-    const size_t smem = (size_t)p.slots * ns * p.stage_bytes + 8 * (size_t)p.slots * ns + tail;
+    const size_t smem = (size_t)p.slots * ns * p.stage_bytes + 16 * (size_t)p.slots * ns + red_b * ns + tail;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -460,22 +497,27 @@ cudaError_t launch_t(GemvParams p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <int BITS>
-cudaError_t dispatch(const GemvParams& p, int NB, int ncpl, cudaStream_t s) {
+template <int BITS, bool LEAN>
+cudaError_t dispatch_nb(const GemvParams& p, int NB, int ncpl, cudaStream_t s) {
     switch (NB) {
-        case 1: return ncpl == 2 ? launch_t<BITS, 1, 2, 2>(p, s) : launch_t<BITS, 1, 1, 4>(p, s);
-        case 2: return ncpl == 2 ? launch_t<BITS, 2, 2, 2>(p, s) : launch_t<BITS, 2, 1, 4>(p, s);
+        case 1: return ncpl == 2 ? launch_t<BITS, 1, 2, 4, LEAN>(p, s) : launch_t<BITS, 1, 1, 8, LEAN>(p, s);
+        case 2: return ncpl == 2 ? launch_t<BITS, 2, 2, 4, LEAN>(p, s) : launch_t<BITS, 2, 1, 4, LEAN>(p, s);
         case 3:
             if constexpr (BITS == 8) {
-                if (ncpl == 2) return launch_t<BITS, 3, 2, 2>(p, s);
+                if (ncpl == 2) return launch_t<BITS, 3, 2, 2, LEAN>(p, s);
             }
-            return launch_t<BITS, 3, 1, 2>(p, s);
+            return launch_t<BITS, 3, 1, 2, LEAN>(p, s);
         default:
             if constexpr (BITS == 8) {
-                if (ncpl == 2) return launch_t<BITS, 4, 2, 2>(p, s);
+                if (ncpl == 2) return launch_t<BITS, 4, 2, 2, LEAN>(p, s);
             }
-            return launch_t<BITS, 4, 1, 2>(p, s);
+            return launch_t<BITS, 4, 1, 2, LEAN>(p, s);
     }
+}
+
+template <int BITS>
+cudaError_t dispatch(const GemvParams& p, int NB, int ncpl, bool lean, cudaStream_t s) {
+    return lean ? dispatch_nb<BITS, true>(p, NB, ncpl, s) : dispatch_nb<BITS, false>(p, NB, ncpl, s);
 }
 
 }  // namespace
@@ -529,7 +571,8 @@ cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t 
     if (!ok) return cudaErrorInvalidValue;
     p.wpr = c.wpr;
     p.slots = c.slots;
-    return g.bits == 4 ? dispatch<4>(p, NB, c.ncpl, s) : dispatch<8>(p, NB, c.ncpl, s);
+    const bool lean = p.bulk_tables && c.wpr * 32 * c.ncpl == p.NCH;
+    return g.bits == 4 ? dispatch<4>(p, NB, c.ncpl, lean, s) : dispatch<8>(p, NB, c.ncpl, lean, s);
 }
 
 }  // namespace wq
