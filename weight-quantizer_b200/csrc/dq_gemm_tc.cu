@@ -24,13 +24,14 @@
 //     scale[m, g] * D into register accumulators, and at the end write
 //     y[n, m] = acc * 2^-S_b.
 //
-// Roles (one CTA = one 128 x BN output tile, 11 warps): warp 0 bulk-copies the
+// Roles (one CTA = one 128 x BN output tile, 12 warps): warp 0 bulk-copies the
 // x' planes into an NS-deep shared-memory ring; warp 10 loads packed codes
 // (several K tiles per 2D TMA box, 128 bytes per row, 128-byte swizzle) into a
 // separate ring that the dequant warps release as soon as they have read it;
 // warp 1 allocates tensor memory and one thread issues tcgen05.mma (M = 128,
-// N = BN, K = 16, A from tensor memory) and tcgen05.commit; warps 2-5
-// dequantize; warps 6-9 run the epilogue. All hand-offs are mbarriers; every
+// N = BN, K = 16, A from tensor memory) and tcgen05.commit, learning which
+// tiles are ready from one shared word that warp 11 publishes after waiting
+// on their barriers; warps 2-5 dequantize; warps 6-9 run the epilogue. All hand-offs are mbarriers; every
 // wait is bounded and, on expiry, records bit 0 in the library's fault word
 // and stops waiting. Every TMA and bulk load targets this CTA's own shared
 // memory only.
@@ -50,9 +51,9 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int kThreads = 352;    // 11 warps
+constexpr int kThreads = 384;    // 12 warps
 constexpr int kBand = 16;        // batch tiles per rasterization band
-constexpr int kWarpB = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 6, kWarpCodes = 10;
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 6, kWarpCodes = 10, kWarpSched = 11;
 constexpr int kCodeRowBytes = 128;  // packed code bytes per row per codes stage
 constexpr int kNC = 2;              // codes stages
 
@@ -192,6 +193,7 @@ struct Smem {
     // c_full, c_empty per codes stage; acc_full[2], acc_empty[2]
     static constexpr int NBAR = 2 * NS + 2 * NA + 2 * kNC + 4;
     static constexpr int TMEM_SLOT = BAR_OFF + 8 * NBAR;
+    static constexpr int READY = TMEM_SLOT + 8;   // u32: tiles whose operands are ready
     static constexpr int TOTAL = TMEM_SLOT + 16;
     static_assert(STAGE % 1024 == 0 && C_STAGE % 1024 == 0, "tiles must stay 1024-byte aligned for the 128-byte swizzle");
     static_assert(TOTAL + 1024 <= 227 * 1024, "stage rings exceed the shared memory of one CTA");
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(acc_full(b), 1);
             mbar_init(acc_empty(b), 4);   // one arrival per epilogue warp
         }
+        *reinterpret_cast<volatile uint32_t*>(smem + L::READY) = 0u;
         fence_mbarrier_init();
     }
     if (warp == kWarpMma) {
@@ -323,13 +326,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             drain(kNC, nct, c_full);
         }
+    } else if (warp == kWarpSched) {
+        // Scheduler: walks the tiles in order, waits for each tile's x' stage,
+        // A stage (first tile of a stage) and accumulator (first tile of a
+        // group), and publishes how many tiles are ready. The MMA thread reads
+        // that one word instead of the barriers: any shared-memory or barrier
+        // operation it issues waits behind its own queued MMAs, so it should
+        // touch as few as possible.
+        if (lane == 0) {
+            int sb = 0, sa = 0, h = 0, gin = 0, g = 0;
+            uint32_t phb = 0, pha = 0;
+            for (int t = 0; t < p.KT; ++t) {
+                const int use = g >> 1;
+                if (gin == 0 && use > 0) wait(acc_empty(g & 1), (uint32_t)((use - 1) & 1));
+                wait(full_b(sb), phb);
+                if (h == 0) wait(full_a(sa), pha);
+                asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(sbase + L::READY), "r"((uint32_t)(t + 1))
+                             : "memory");
+                if ((gin == p.ktg - 1) || (t == p.KT - 1)) {
+                    gin = 0;
+                    ++g;
+                } else {
+                    ++gin;
+                }
+                if (++sb == NS) {
+                    sb = 0;
+                    phb ^= 1u;
+                }
+                if (++h == kTilesPerA) {
+                    h = 0;
+                    if (++sa == NA) {
+                        sa = 0;
+                        pha ^= 1u;
+                    }
+                }
+            }
+        }
     } else if (warp == kWarpMma) {
-        // One thread issues every MMA. Any shared-memory or barrier operation
-        // this thread issues waits behind its own queued tcgen05.mma
-        // instructions, so each wait point costs a pipeline drain. The thread
-        // therefore waits (blocking) only for the next tile, then probes the
-        // following tiles without blocking and issues every tile that is
-        // ready, up to kIssueBatch, before it touches a barrier again.
+        // One thread issues every MMA: it reads the scheduler's ready count,
+        // then issues every ready tile (up to kIssueBatch) back to back.
         // A comes from tensor memory; B descriptors are built once and a
         // stage, a plane or a 16-wide K step only moves the start-address
         // field (address / 16 in bits 0-13).
@@ -339,74 +374,50 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             const uint64_t b_desc0 = sw128_desc(stage_b(0));
             constexpr uint64_t kPlaneStep = (uint64_t)(L::B_BYTES >> 4);
-            // per-tile pipeline position; advance() moves it to the next tile
-            struct Pos {
-                int t, sb, sa, h, gin, g;
-                uint32_t phb, pha;
-            };
-            auto advance = [&](Pos& x) {
-                const bool last = (x.gin == p.ktg - 1) || (x.t == p.KT - 1);
-                if (last) {
-                    x.gin = 0;
-                    ++x.g;
-                } else {
-                    ++x.gin;
+            int t = 0, sb = 0, sa = 0, h = 0, gin = 0, g = 0;
+            while (t < p.KT) {
+                uint32_t ready = 0;
+                uint32_t polls = 0;
+                for (;;) {
+                    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(ready) : "r"(sbase + L::READY)
+                                 : "memory");
+                    if ((int)ready > t) break;
+                    if (++polls == kMaxPolls) break;
                 }
-                if (++x.sb == NS) {
-                    x.sb = 0;
-                    x.phb ^= 1u;
+                if ((int)ready <= t) {   // the scheduler stalled: give up on the rest of the tile
+                    atomicOr(p.fault, 1u);
+                    faulted = true;
+                    break;
                 }
-                if (++x.h == kTilesPerA) {
-                    x.h = 0;
-                    if (++x.sa == NA) {
-                        x.sa = 0;
-                        x.pha ^= 1u;
-                    }
-                }
-                ++x.t;
-            };
-            // the barriers tile x needs: its x' stage, its A stage (first
-            // tile of the stage), its accumulator (first tile of a group)
-            auto ready = [&](const Pos& x, bool block) -> bool {
-                const int use = x.g >> 1;
-                if (x.gin == 0 && use > 0) {
-                    const uint32_t b = acc_empty(x.g & 1), par = (uint32_t)((use - 1) & 1);
-                    if (block) wait(b, par); else if (!mbar_test_wait(b, par)) return false;
-                }
-                if (block) wait(full_b(x.sb), x.phb); else if (!mbar_test_wait(full_b(x.sb), x.phb)) return false;
-                if (x.h == 0) {
-                    if (block) wait(full_a(x.sa), x.pha); else if (!mbar_test_wait(full_a(x.sa), x.pha)) return false;
-                }
-                return true;
-            };
-            Pos cur{0, 0, 0, 0, 0, 0, 0u, 0u};
-            while (cur.t < p.KT) {
-                ready(cur, true);
-                int n = 1;
-                Pos probe = cur;
-                advance(probe);
-                while (n < kIssueBatch && probe.t < p.KT && !faulted && ready(probe, false)) {
-                    ++n;
-                    advance(probe);
-                }
+                const int n = min((int)ready - t, kIssueBatch);
                 tc_fence_after();
-                for (int i = 0; i < n; ++i) {
-                    const bool first = cur.gin == 0;
-                    const bool last = (cur.gin == p.ktg - 1) || (cur.t == p.KT - 1);
-                    const int buf = cur.g & 1;
+                for (int i = 0; i < n; ++i, ++t) {
+                    const bool first = gin == 0;
+                    const bool last = (gin == p.ktg - 1) || (t == p.KT - 1);
+                    const int buf = g & 1;
                     const uint32_t d = tmem + (uint32_t)(buf * BN);
-                    const uint32_t a_tile = tmem_a0 + (uint32_t)(cur.sa * kAStageCols + cur.h * (BK / 2));
-                    const uint64_t b_desc = b_desc0 + (uint64_t)(cur.sb * (L::STAGE >> 4));
+                    const uint32_t a_tile = tmem_a0 + (uint32_t)(sa * kAStageCols + h * (BK / 2));
+                    const uint64_t b_desc = b_desc0 + (uint64_t)(sb * (L::STAGE >> 4));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t bd = b_desc + 2u * kk;
                         mma_f16_ts(d, a_tile + 8u * kk, bd, idesc, (first && kk == 0) ? 0u : 1u);
                         mma_f16_ts(d, a_tile + 8u * kk, bd + kPlaneStep, idesc, 1u);
                     }
-                    mma_commit(empty_b(cur.sb));
-                    if (last) mma_commit(acc_full(buf));
-                    if (cur.h == kTilesPerA - 1 || cur.t == p.KT - 1) mma_commit(empty_a(cur.sa));
-                    advance(cur);
+                    mma_commit(empty_b(sb));
+                    if (last) {
+                        mma_commit(acc_full(buf));
+                        gin = 0;
+                        ++g;
+                    } else {
+                        ++gin;
+                    }
+                    if (h == kTilesPerA - 1 || t == p.KT - 1) mma_commit(empty_a(sa));
+                    if (++sb == NS) sb = 0;
+                    if (++h == kTilesPerA) {
+                        h = 0;
+                        if (++sa == NA) sa = 0;
+                    }
                 }
             }
             drain(NS, p.KT, empty_b);
