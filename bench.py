@@ -237,7 +237,10 @@ def ours(args: argparse.Namespace) -> None:
             granularity="group")
     lin = sharded.RowParallelDequantLinear(shard, M_ROWS, rank, world)
     weight_bytes_job = (M_ROWS * (K_COLS // 2)) + 2 * 4 * M_ROWS * (K_COLS // GROUP)
-    launches_per_step = 1 + (1 if world > 1 else 0)
+    # our kernels per step: batch >= 5 runs the x' prep kernel and the
+    # tensor-core kernel, batch <= 4 the decode kernel alone; N > 1 adds the
+    # gather-permute kernel (the all-gather itself is NCCL's)
+    launches_per_step = (2 if args.batch > 4 else 1) + (1 if world > 1 else 0)
 
     stream = torch.cuda.current_stream(dev)
     B = args.batch
@@ -277,13 +280,27 @@ def ours(args: argparse.Namespace) -> None:
     t_kernel = sum(a.elapsed_time(b) for a, b in kt) / len(kt) / 1e3
     kernel_flops = 2.0 * B * mp * K_COLS
     achieved_tflops = kernel_flops / t_kernel / 1e12
+    # DRAM bytes (read + write) of one tensor-core launch at batch 4096 on one
+    # GPU, from the ncu capture summarised in profiles/dq_gemm_tc_28672x8192_b4096.md
+    traffic = 2.700058e9 + 0.510467e9 if (B == 4096 and world == 1) else None
     roofline = {"bound": "tensor", "achieved": round(achieved_tflops, 3), "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4), "traffic": None,
-                "kernel": "dequant-GEMM (batch %d, %d rows per GPU)" % (B, mp),
+                "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
+                "traffic_unit": "bytes per launch",
+                "kernel": "dequant-GEMM (batch %d, %d rows per GPU; the timed call is the x' prep kernel "
+                          "plus the tensor-core kernel)" % (B, mp),
                 "kernel_ms": round(t_kernel * 1e3, 4), "peak_source": peaks["source"]}
 
     # ---- sweep: decode batches, L2 flushed between iterations --------------
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    # The flush writes one 256 MB buffer and then reads another, so L2 holds
+    # none of the layer's data and no dirty lines whose write-back would
+    # compete with the timed kernel's reads.
+    flush_w = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_r = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def flush_l2(i: int) -> None:
+        flush_w.fill_(float(i))
+        flush_r.sum()
+
     sweep = []
     for b in args.sweep:
         if b == B:
@@ -293,7 +310,7 @@ def ours(args: argparse.Namespace) -> None:
             lin.forward(xb)
         ts = []
         for _ in range(args.steps):
-            flush.zero_()
+            flush_l2(len(ts))
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             barrier()
             e0.record(stream)
@@ -304,7 +321,7 @@ def ours(args: argparse.Namespace) -> None:
         t = max_over_ranks(statistics.median(a.elapsed_time(c) for a, c in ts) / 1e3)
         kt2 = []
         for _ in range(args.steps):
-            flush.zero_()
+            flush_l2(len(kt2))
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             lin.forward_local(xb, out=local_out[:b])
@@ -363,13 +380,14 @@ def ours(args: argparse.Namespace) -> None:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 hi/lo -> f32",
             "data": "synthetic (seeded: W ~ N(0, 0.015), x ~ N(0, 1))",
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_COLS, "batch": B, "bits": 4,
                        "group_size": GROUP, "symmetric": True,
                        "parallelism": f"row-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
                        "l2": "working set larger than L2 (x 134 MB, y 470 MB, weights 132 MB at batch 4096); "
-                             "sweep lines flush L2 (256 MB write) between iterations"},
+                             "sweep lines flush L2 (256 MB write, then a 256 MB read of another buffer) "
+                             "between iterations"},
             "weight_gbs": round(weight_bytes_job / t_step / 1e9, 1),
             "clocks": {"sm_mhz": clock["sm_mhz"], "sm_max_mhz": clock["sm_max_mhz"], "reasons": clock["reasons"]},
             "roofline": roofline,
