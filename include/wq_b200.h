@@ -67,7 +67,8 @@ enum wq_status {
     WQ_E_INT4_RANGE = 18,    /* "int4 codes must lie in [0, 15]" (pack.py:22-26) */
     WQ_E_GROUP_MODE = 19,    /* "group_size must be None, 0, or positive" (quant.py:75-76) */
     WQ_E_LD = 20,            /* output row stride smaller than the row length */
-    WQ_E_NOALLOC_LIMIT = 21  /* problem needs more scratch than wq_dequant_gemm_f32_noalloc holds */
+    WQ_E_NOALLOC_LIMIT = 21, /* problem needs more scratch than wq_dequant_gemm_f32_noalloc holds */
+    WQ_E_OUTPUTS = 22        /* output count outside [1, WQ_MAX_OUTPUTS] */
 };
 
 /* Message for a status code (static storage; never NULL). */
@@ -191,6 +192,46 @@ WQ_API int wq_dequantize_f32(const uint8_t* q, int64_t M, int64_t K, int64_t q_c
  * row-sharded outputs (each of P ranks produced y[:, p*Mp:(p+1)*Mp]). */
 WQ_API int wq_gather_permute_f32(const float* src, int64_t P, int64_t B, int64_t Mp,
                           float* dst, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */
+/* whose kernel runs on one CPU and splits rows across OpenMP threads        */
+/* (dequant_gemm.cpp:196-205). Each rank computes its rows of y; the         */
+/* tensor-core kernel's epilogue stores every finished value into the full   */
+/* y buffer of every rank (its own and its peers', mapped with the IPC calls */
+/* below), so the exchange over NVLink overlaps the computation and no       */
+/* gather or permute pass follows. The caller orders the ranks around the    */
+/* call (every rank done reading its y before any rank starts, and every     */
+/* rank's call complete before y is read), e.g. with a one-element NCCL      */
+/* all-reduce on each side of it.                                            */
+/* ------------------------------------------------------------------------ */
+#define WQ_MAX_OUTPUTS 8
+
+/* Bytes of an IPC handle (cudaIpcMemHandle_t). */
+WQ_API size_t wq_ipc_handle_bytes(void);
+/* Handle of the device allocation that contains `ptr`, and ptr's byte offset
+ * inside that allocation (caching allocators hand out interior pointers). */
+WQ_API int wq_ipc_get_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+/* Maps another process's allocation into this one (peer access enabled
+ * lazily); *ptr_out = mapped base + offset. */
+WQ_API int wq_ipc_open_handle(const void* handle, int64_t offset, void** ptr_out);
+/* Unmaps a pointer returned by wq_ipc_open_handle with the same offset. */
+WQ_API int wq_ipc_close_handle(void* ptr, int64_t offset);
+
+/* wq_dequant_gemm_f32 with the output written to n_out buffers (1 <= n_out
+ * <= WQ_MAX_OUTPUTS, a host array of device pointers, local or peer-mapped),
+ * each holding the [B, M] result at row stride ldy. The tensor-core path
+ * stores into all of them from its epilogue; the other paths compute into
+ * y_out[0] and copy it to the rest on the same stream. */
+WQ_API int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
+                                     const uint8_t* q, int64_t M, int64_t q_cols,
+                                     const float* scales, int64_t scale_rows, int64_t groups,
+                                     const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                                     const float* channel_scale, int64_t channel_len,
+                                     int group_size, int bits,
+                                     float* const* y_out, int n_out, int64_t ldy,
+                                     void* workspace, size_t workspace_bytes,
+                                     void* stream);
 
 #ifdef __cplusplus
 }

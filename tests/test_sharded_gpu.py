@@ -1,5 +1,6 @@
 """Row-sharded dequant-GEMM on GPUs: the permute kernel, the one-rank layer, and
-(with two or more GPUs) the NCCL path compared with the unsharded layer."""
+(with two or more GPUs) the NCCL and peer-store exchanges compared with the
+unsharded layer."""
 
 from __future__ import annotations
 
@@ -69,11 +70,18 @@ def _nccl_worker(rank: int, world: int, port: int, out_dir: str) -> None:
         scales=torch.cat((full_rows.scales, torch.ones(pad, K // 128, device=dev))),
         zeros=torch.cat((full_rows.zeros, torch.zeros(pad, K // 128, device=dev))),
         bits=4, group_size=128, in_features=K, out_features=mp_, symmetric=True, packed=True, granularity="group")
-    lin = sharded.RowParallelDequantLinear(shard, M, rank, world)
+    lin = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="nccl")
+    p2p = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="p2p")
     for b in (1, 64):
         x = torch.randn(b, K, generator=g).to(dev)
         y = lin.forward(x)
         np.save(os.path.join(out_dir, f"y{rank}_b{b}.npy"), y.cpu().numpy())
+        for rep in range(2):   # the second call reuses the mapped peer buffers
+            y2 = p2p.forward(x)
+            np.save(os.path.join(out_dir, f"p2p{rank}_b{b}_{rep}.npy"), y2.cpu().numpy())
+    torch.cuda.synchronize()
+    dist.barrier()
+    p2p.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -91,4 +99,8 @@ def test_row_parallel_nccl_matches_unsharded(wq, cuda, tmp_path) -> None:
         x = torch.randn(b, K, generator=g).to(cuda)
         expect = wq.dequant_gemm(x, qw, impl="kernel").cpu().numpy()
         for r in range(world):
-            assert_close_y(np.load(tmp_path / f"y{r}_b{b}.npy"), expect, f"rank {r} b{b}")
+            got = np.load(tmp_path / f"y{r}_b{b}.npy")
+            assert_close_y(got, expect, f"rank {r} b{b}")
+            # the peer-store exchange delivers the same values bit for bit
+            for rep in range(2):
+                assert np.array_equal(np.load(tmp_path / f"p2p{r}_b{b}_{rep}.npy"), got), (r, b, rep)

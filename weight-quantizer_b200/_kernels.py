@@ -24,7 +24,7 @@ LIB_PATH = os.path.join(_HERE, "libwq_b200.so")
 
 WQ_OK = 0
 WQ_E_CUDA = 14
-_ARG_ERRORS_AS_VALUEERROR = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15, 16, 17, 18, 19, 20, 21}
+_ARG_ERRORS_AS_VALUEERROR = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 15, 16, 17, 18, 19, 20, 21, 22}
 
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -60,7 +60,18 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
          _int, _int, _vp, _i64, _vp],
     ),
+    "wq_ipc_handle_bytes": (_sz, []),
+    "wq_ipc_get_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int64)]),
+    "wq_ipc_open_handle": (_int, [_vp, _i64, ctypes.POINTER(ctypes.c_void_p)]),
+    "wq_ipc_close_handle": (_int, [_vp, _i64]),
+    "wq_dequant_gemm_f32_multi": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
+         _int, _int, _vp, _int, _i64, _vp, _sz, _vp],
+    ),
 }
+
+MAX_OUTPUTS = 8
 
 
 class _KernelInfo(ctypes.Structure):
@@ -340,3 +351,76 @@ def gather_permute(src: torch.Tensor, parts: int, out: torch.Tensor | None = Non
     dst = out if out is not None else torch.empty((B, P * Mp), dtype=torch.float32, device=dev)
     _check(library().wq_gather_permute_f32(_ptr(s), P, B, Mp, _ptr(dst), _stream(dev)))
     return dst
+
+
+def dequant_gemm_multi(
+    x: torch.Tensor,
+    q: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    channel_scale: torch.Tensor | None,
+    group_size: int,
+    bits: int,
+    outputs: list[int],
+    ldy: int,
+) -> None:
+    """dequant_gemm writing the same [B, M] result (row stride ``ldy``) into
+    every device pointer of ``outputs`` (this GPU's buffers or peer buffers
+    mapped with :func:`ipc_open`). The first output must be on the inputs'
+    device; the tensor-core path stores into all of them from its epilogue."""
+    if x.ndim != 2:
+        raise ValueError("x must have shape [B, K]")
+    if q.ndim != 2 or scales.ndim != 2 or zeros.ndim != 2:
+        raise ValueError("q, scales, and zeros must be rank 2")
+    if not 1 <= len(outputs) <= MAX_OUTPUTS:
+        raise ValueError(f"between 1 and {MAX_OUTPUTS} outputs")
+    tensors = [x, q, scales, zeros] + ([] if channel_scale is None else [channel_scale])
+    dev = _cuda_device(tensors)
+    x = x.to(dtype=torch.float32).contiguous()
+    q = q.to(dtype=torch.uint8).contiguous()
+    scales = scales.to(dtype=torch.float32).contiguous()
+    zeros = zeros.to(dtype=torch.float32).contiguous()
+    ch_len = -1
+    if channel_scale is not None:
+        channel_scale = channel_scale.to(dtype=torch.float32).contiguous()
+        ch_len = int(channel_scale.shape[0])
+    B, K = int(x.shape[0]), int(x.shape[1])
+    M = int(q.shape[0])
+    lib = library()
+    ws_bytes = int(lib.wq_dequant_gemm_workspace_bytes(B, M, K, int(group_size), int(bits)))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+    arr = (ctypes.c_void_p * len(outputs))(*[ctypes.c_void_p(int(o)) for o in outputs])
+    status = lib.wq_dequant_gemm_f32_multi(
+        _ptr(x), B, K,
+        _ptr(q), M, int(q.shape[1]),
+        _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
+        _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
+        _ptr(channel_scale), ch_len,
+        int(group_size), int(bits),
+        ctypes.cast(arr, ctypes.c_void_p), len(outputs), int(ldy),
+        _ptr(ws), ws_bytes,
+        _stream(dev),
+    )
+    _check(status)
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """IPC handle of the device allocation holding ``t`` and t's byte offset in it."""
+    lib = library()
+    n = int(lib.wq_ipc_handle_bytes())
+    buf = ctypes.create_string_buffer(n)
+    off = ctypes.c_int64(0)
+    _check(lib.wq_ipc_get_handle(ctypes.c_void_p(t.data_ptr()), buf, ctypes.byref(off)))
+    return bytes(buf.raw), int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Maps another process's allocation; returns the device pointer at ``offset``."""
+    lib = library()
+    ptr = ctypes.c_void_p(0)
+    _check(lib.wq_ipc_open_handle(ctypes.c_char_p(handle), int(offset), ctypes.byref(ptr)))
+    return int(ptr.value or 0)
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    _check(library().wq_ipc_close_handle(ctypes.c_void_p(int(ptr)), int(offset)))

@@ -2,6 +2,8 @@
 // with the messages of ptqkit's pybind11 entry point
 // (src/ptqkit/csrc/dequant_gemm.cpp:222-300), then dispatch to the kernels.
 // Nothing here allocates device memory or synchronizes the host.
+#include <cuda.h>
+
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -84,6 +86,7 @@ const char* wq_status_string(int status) {
         case WQ_E_LD: return "output row stride is smaller than the output row length";
         case WQ_E_NOALLOC_LIMIT:
             return "problem needs more scratch than the no-allocation entry point holds; use wq_dequant_gemm_f32";
+        case WQ_E_OUTPUTS: return "output count must be between 1 and WQ_MAX_OUTPUTS";
         default: return "unknown status";
     }
 }
@@ -129,15 +132,16 @@ size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int grou
     return 0;
 }
 
-int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
-                        const uint8_t* q, int64_t M, int64_t q_cols,
-                        const float* scales, int64_t scale_rows, int64_t groups,
-                        const float* zeros, int64_t zero_rows, int64_t zero_groups,
-                        const float* channel_scale, int64_t channel_len,
-                        int group_size, int bits,
-                        float* y, int64_t ldy,
-                        void* workspace, size_t workspace_bytes,
-                        void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Validation in the reference's order, then dispatch; y_out[0] is the primary
+// output, y_out[1..n_out) receive the same values.
+int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, int64_t q_cols,
+             const float* scales, int64_t scale_rows, int64_t groups, const float* zeros, int64_t zero_rows,
+             int64_t zero_groups, const float* channel_scale, int64_t channel_len, int group_size, int bits,
+             float* const* y_out, int n_out, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
     // dequant_gemm.cpp:241-276, same order
     if (bits != 4 && bits != 8) return WQ_E_BITS;
     if (group_size <= 0) return WQ_E_GROUP_SIZE;
@@ -149,15 +153,21 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
     const int64_t n_groups = K == 0 ? 0 : (K + group_size - 1) / group_size;
     if (K > 0 && groups != n_groups) return WQ_E_SCALE_GROUPS;
     if (channel_scale != nullptr && channel_len != K) return WQ_E_CHANNEL_SHAPE;
-    // beyond the reference: output stride, pointers, index range
+    // beyond the reference: output count and stride, pointers, index range
+    if (n_out < 1 || n_out > WQ_MAX_OUTPUTS) return WQ_E_OUTPUTS;
     if (ldy < M) return WQ_E_LD;
     if (B > kMaxDim || M > kMaxDim || K > kMaxDim || groups > kMaxDim) return WQ_E_TOO_LARGE;
     if (B == 0 || M == 0) return WQ_OK;
-    if (y == nullptr) return WQ_E_NULL;
+    if (y_out == nullptr) return WQ_E_NULL;
+    for (int i = 0; i < n_out; ++i)
+        if (y_out[i] == nullptr) return WQ_E_NULL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (K == 0) {
-        cudaError_t e = wq::launch_fill_zero(y, B, M, ldy, s);
-        return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+        for (int i = 0; i < n_out; ++i) {
+            cudaError_t e = wq::launch_fill_zero(y_out[i], B, M, ldy, s);
+            if (e != cudaSuccess) return cuda_fail(e);
+        }
+        return WQ_OK;
     }
     if (x == nullptr || q == nullptr || scales == nullptr || zeros == nullptr) return WQ_E_NULL;
 
@@ -167,7 +177,9 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
     p.scales = scales;
     p.zeros = zeros;
     p.channel = channel_scale;
-    p.y = y;
+    p.y = y_out[0];
+    p.n_extra = 0;
+    for (int i = 0; i < 7; ++i) p.y_extra[i] = nullptr;
     p.B = B;
     p.M = M;
     p.K = K;
@@ -179,6 +191,7 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
     p.bits = bits;
 
     cudaError_t e;
+    bool copies = n_out > 1;   // paths without a multi-output epilogue copy afterwards
     if (wq::gemv_supported(p)) {
         const size_t need = wq::gemv_workspace_bytes(B, K, bits);
         if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
@@ -187,10 +200,103 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
         const size_t need = wq::tc_workspace_bytes(B, K);
         if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
         if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
+        p.n_extra = n_out - 1;
+        for (int i = 1; i < n_out; ++i) p.y_extra[i - 1] = y_out[i];
+        copies = false;
         e = wq::launch_tc(p, workspace, s);
     } else {
         e = wq::launch_gemm_simt(p, s);
     }
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (copies) {
+        for (int i = 1; i < n_out; ++i) {
+            e = cudaMemcpy2DAsync(y_out[i], (size_t)ldy * sizeof(float), y_out[0], (size_t)ldy * sizeof(float),
+                                  (size_t)M * sizeof(float), (size_t)B, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e);
+        }
+    }
+    return WQ_OK;
+}
+
+using MemGetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+MemGetAddressRangeFn address_range_fn() {
+    static MemGetAddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<MemGetAddressRangeFn>(ptr);
+    });
+    return fn;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
+                        const uint8_t* q, int64_t M, int64_t q_cols,
+                        const float* scales, int64_t scale_rows, int64_t groups,
+                        const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                        const float* channel_scale, int64_t channel_len,
+                        int group_size, int bits,
+                        float* y, int64_t ldy,
+                        void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    float* const outs[1] = {y};
+    return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
+                    channel_len, group_size, bits, y == nullptr ? nullptr : outs, 1, ldy, workspace,
+                    workspace_bytes, stream);
+}
+
+int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
+                              const uint8_t* q, int64_t M, int64_t q_cols,
+                              const float* scales, int64_t scale_rows, int64_t groups,
+                              const float* zeros, int64_t zero_rows, int64_t zero_groups,
+                              const float* channel_scale, int64_t channel_len,
+                              int group_size, int bits,
+                              float* const* y_out, int n_out, int64_t ldy,
+                              void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
+                    channel_len, group_size, bits, y_out, n_out, ldy, workspace, workspace_bytes, stream);
+}
+
+size_t wq_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int wq_ipc_get_handle(const void* ptr, void* handle_out, int64_t* offset_out) {
+    if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr) return WQ_E_NULL;
+    MemGetAddressRangeFn range = address_range_fn();
+    if (range == nullptr) return cuda_fail(cudaErrorNotSupported);
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e);
+    std::memcpy(handle_out, &h, sizeof(h));
+    *offset_out = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return WQ_OK;
+}
+
+int wq_ipc_open_handle(const void* handle, int64_t offset, void** ptr_out) {
+    if (handle == nullptr || ptr_out == nullptr) return WQ_E_NULL;
+    if (offset < 0) return WQ_E_NEG_DIM;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *ptr_out = static_cast<unsigned char*>(base) + offset;
+    return WQ_OK;
+}
+
+int wq_ipc_close_handle(void* ptr, int64_t offset) {
+    if (ptr == nullptr) return WQ_E_NULL;
+    cudaError_t e = cudaIpcCloseMemHandle(static_cast<unsigned char*>(ptr) - offset);
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 

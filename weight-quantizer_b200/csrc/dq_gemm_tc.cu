@@ -63,6 +63,8 @@ struct TcParams {
     const float* zeros;
     const float* inv_s;   // [B] 2^-S_b
     float* y;
+    float* y_extra[7];    // further outputs with y's layout (peer-mapped on other GPUs)
+    int n_extra;
     unsigned int* fault;
     int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
@@ -433,12 +435,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t swz = (uint32_t)(r & 7);
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         bool inexact = false;
-        // Zero points of groups g + 1 and g + 2 are in flight while group g is
-        // processed (an L2 round trip is longer than one K tile).
+        // Zero points of groups g + 1 .. g + 4 are in flight while group g is
+        // processed: every thread reads its own row, so these loads are not
+        // coalesced and take longer than a few K tiles under load.
         const float* zrow = p.zeros + srow * p.groups;
         float z_cur = __ldg(zrow);
         float z_n1 = p.ngroups > 1 ? __ldg(zrow + 1) : 0.0f;
         float z_n2 = p.ngroups > 2 ? __ldg(zrow + 2) : 0.0f;
+        float z_n3 = p.ngroups > 3 ? __ldg(zrow + 3) : 0.0f;
+        float z_n4 = p.ngroups > 4 ? __ldg(zrow + 4) : 0.0f;
         int sa = 0, c = 0, kin = 0, gin = 0, g = 0;
         uint32_t pha = 0, cph = 0;
         int t = 0;
@@ -452,7 +457,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++g;
                     z_cur = z_n1;
                     z_n1 = z_n2;
-                    if (g + 2 < p.ngroups) z_n2 = __ldg(zrow + g + 2);
+                    z_n2 = z_n3;
+                    z_n3 = z_n4;
+                    if (g + 4 < p.ngroups) z_n4 = __ldg(zrow + g + 4);
                 }
                 const float z = z_cur;
                 const float zb = 1024.0f + z;
@@ -520,10 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[BN];
 #pragma unroll
         for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
-        // scales of groups g + 1 and g + 2 are in flight while group g is read
+        // scales of groups g + 1 .. g + 4 are in flight while group g is read
         const float* srow_p = p.scales + srow * p.groups;
         float sc_n1 = p.ngroups > 1 ? __ldg(srow_p + 1) : 0.0f;
         float sc_n2 = p.ngroups > 2 ? __ldg(srow_p + 2) : 0.0f;
+        float sc_n3 = p.ngroups > 3 ? __ldg(srow_p + 3) : 0.0f;
+        float sc_n4 = p.ngroups > 4 ? __ldg(srow_p + 4) : 0.0f;
         float sc = __ldg(srow_p);
         for (int g = 0; g < p.ngroups; ++g) {
             const int buf = g & 1, use = g >> 1;
@@ -542,13 +551,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(acc_empty(buf));
             sc = sc_n1;
             sc_n1 = sc_n2;
-            if (g + 3 < p.ngroups) sc_n2 = __ldg(srow_p + g + 3);
+            sc_n2 = sc_n3;
+            sc_n3 = sc_n4;
+            if (g + 5 < p.ngroups) sc_n4 = __ldg(srow_p + g + 5);
         }
         if (m < p.M) {
+            // Every output buffer gets the tile; stores to peer-mapped buffers
+            // travel over NVLink while other tiles still compute. No fence:
+            // the kernel's completion makes its peer stores visible to work
+            // ordered after it, and the caller orders the ranks after the call.
+            for (int d = 0; d <= p.n_extra; ++d) {
+                float* dst = d == 0 ? p.y : p.y_extra[d - 1];
 #pragma unroll
-            for (int i = 0; i < BN; ++i) {
-                const int n = n0 + i;
-                if (n < p.B) p.y[(int64_t)n * p.ldy + m] = acc[i] * __ldg(p.inv_s + n);
+                for (int i = 0; i < BN; ++i) {
+                    const int n = n0 + i;
+                    if (n < p.B) dst[(int64_t)n * p.ldy + m] = acc[i] * __ldg(p.inv_s + n);
+                }
             }
         }
     }
@@ -684,6 +702,8 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.zeros = g.zeros;
     p.inv_s = w.inv_s;
     p.y = g.y;
+    p.n_extra = g.n_extra;
+    for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;
     p.M = (int)g.M;

@@ -15,6 +15,8 @@ struct GemmProblem {
     const float* zeros;    // [scale_rows, groups]
     const float* channel;  // [K] or nullptr
     float* y;              // [B, ldy]
+    float* y_extra[7];     // further outputs with y's layout (peer-mapped or local)
+    int n_extra;           // entries of y_extra in use
     int64_t B, M, K;
     int64_t q_stride;      // bytes per stored row: K (int8) or (K+1)/2 (int4)
     int64_t ldy;

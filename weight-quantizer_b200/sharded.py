@@ -5,10 +5,16 @@ ptqkit splits the output rows of a layer across OpenMP threads
 GPUs, one process per GPU: rank r owns rows [r*Mp, (r+1)*Mp) of the packed
 codes and of the scale/zero tables (Mp = ceil(M / world); the last shard is
 padded with rows whose output is dropped), while x and the channel scale are
-replicated. Each rank computes its y shard with the local kernel; when the
-whole y is needed, one NCCL all-gather over NVLink collects the shards as
-[world, B, Mp] and a permute kernel lays them out as [B, M]. Per-tensor
-granularity (one scale for all rows) is replicated on every rank.
+replicated. Per-tensor granularity (one scale for all rows) is replicated on
+every rank. When the whole y is needed on every rank there are two exchanges:
+
+* ``exchange="p2p"`` (default on GPUs): every rank maps the other ranks' full
+  y buffers [B, world*Mp] once (CUDA IPC over NVLink) and the dequant-GEMM's
+  epilogue stores each finished value into all of them, so the exchange
+  overlaps the computation; one-element NCCL all-reduces before and after the
+  call order the ranks around it.
+* ``exchange="nccl"``: the kernel writes the local shard, one NCCL all-gather
+  collects [world, B, Mp] and a permute kernel lays it out as [B, M].
 """
 
 from __future__ import annotations
@@ -70,7 +76,7 @@ class RowParallelDequantLinear:
     """One rank's part of a row-sharded quantized linear layer (no bias)."""
 
     def __init__(self, shard: QuantizedWeight, out_features: int, rank: int, world: int,
-                 group: dist.ProcessGroup | None = None) -> None:
+                 group: dist.ProcessGroup | None = None, exchange: str = "p2p") -> None:
         mp, _ = shard_rows(out_features, world)
         if shard.out_features != mp:
             raise ValueError("shard height does not match the row split")
@@ -82,7 +88,12 @@ class RowParallelDequantLinear:
         self.world = world
         self.group = group
         self.mp = mp
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        self.exchange = exchange
         self._bufs: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+        # batch -> (full y, output pointers (own first), opened (ptr, offset) list, sync word)
+        self._peer: dict[int, tuple[torch.Tensor, list[int], list[tuple[int, int]], torch.Tensor]] = {}
 
     def _buffers(self, batch: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         if batch not in self._bufs:
@@ -98,9 +109,49 @@ class RowParallelDequantLinear:
         s = self.shard
         return _kernels.dequant_gemm(x, s.codes, s.scales, s.zeros, s.channel_scale, s.group_size, s.bits, out=out)
 
+    def _peer_buffers(self, batch: int) -> tuple[torch.Tensor, list[int], list[tuple[int, int]], torch.Tensor]:
+        """Full y [B, world*Mp] on this rank and the pointers at which this
+        rank's columns start in every rank's full y (own buffer first)."""
+        if batch not in self._peer:
+            dev = self.shard.codes.device
+            full = torch.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
+            handle = _kernels.ipc_handle(full)
+            handles: list[tuple[bytes, int] | None] = [None] * self.world
+            dist.all_gather_object(handles, handle, group=self.group)
+            col = self.rank * self.mp * 4
+            outs = [full.data_ptr() + col]
+            opened: list[tuple[int, int]] = []
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                h = handles[r]
+                assert h is not None
+                ptr = _kernels.ipc_open(h[0], h[1])
+                opened.append((ptr, h[1]))
+                outs.append(ptr + col)
+            sync = torch.zeros(1, dtype=torch.float32, device=dev)
+            self._peer[batch] = (full, outs, opened, sync)
+        return self._peer[batch]
+
+    def close(self) -> None:
+        """Unmaps the peers' y buffers (every rank calls it; the mappings also
+        end with the process)."""
+        for _, _, opened, _ in self._peer.values():
+            for ptr, off in opened:
+                _kernels.ipc_close(ptr, off)
+        self._peer.clear()
+
     def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
         """y [B, M] on every rank (gather=True), else this rank's [B, Mp] shard."""
         batch = int(x.shape[0])
+        if gather and self.world > 1 and self.exchange == "p2p":
+            full, outs, _, sync = self._peer_buffers(batch)
+            s = self.shard
+            dist.all_reduce(sync, group=self.group)   # every rank is done with its previous y
+            _kernels.dequant_gemm_multi(x, s.codes, s.scales, s.zeros, s.channel_scale, s.group_size, s.bits,
+                                        outs, self.world * self.mp)
+            dist.all_reduce(sync, group=self.group)   # every rank's rows have landed in every y
+            return full[:, : self.out_features]
         local, gathered, full = self._buffers(batch)
         self.forward_local(x, out=local)
         if not gather:
