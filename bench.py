@@ -3,8 +3,9 @@
 Workload: the sharded 28672x8192 int4 symmetric g128 layer (W ~ N(0, 0.015),
 x ~ N(0, 1), seeded synthetic data; weight-quantizer_b200/workloads.py), at
 batch 4096 by default. One step = the layer applied to one batch: each rank
-runs the dequant-GEMM on its row shard, and for N > 1 the shards are
-all-gathered over NVLink (NCCL) and permuted into y [B, M] on every rank.
+runs the dequant-GEMM on its row shard, and for N > 1 the kernel's epilogue
+stores its rows into the full y [B, M] of every rank over NVLink peer memory
+(one-element NCCL all-reduces before and after order the ranks).
 
 Metric: GFLOP/s = 2*B*M*K / t (the reference's convention,
 src/ptqkit/measure.py:167, dequantization not counted), whole job, t = max over
@@ -238,9 +239,10 @@ def ours(args: argparse.Namespace) -> None:
     lin = sharded.RowParallelDequantLinear(shard, M_ROWS, rank, world)
     weight_bytes_job = (M_ROWS * (K_COLS // 2)) + 2 * 4 * M_ROWS * (K_COLS // GROUP)
     # our kernels per step: batch >= 5 runs the x' prep kernel and the
-    # tensor-core kernel, batch <= 4 the decode kernel alone; N > 1 adds the
-    # gather-permute kernel (the all-gather itself is NCCL's)
-    launches_per_step = (2 if args.batch > 4 else 1) + (1 if world > 1 else 0)
+    # tensor-core kernel, batch <= 4 the decode kernel alone; for N > 1 the
+    # tensor-core epilogue stores into every rank's y (the one-element
+    # all-reduces that order the ranks are NCCL's)
+    launches_per_step = 2 if args.batch > 4 else 1
 
     stream = torch.cuda.current_stream(dev)
     B = args.batch
@@ -368,7 +370,7 @@ def ours(args: argparse.Namespace) -> None:
                "h2d_bytes_per_step": int(world * B * K_COLS * 4), "d2h_bytes_per_step": int(B * M_ROWS * 4),
                "ms_per_step": round(t_e2e * 1e3, 3),
                "path": "pinned x -> device, RowParallelDequantLinear.forward (dequant_gemm kernel"
-                       + (" + NCCL all-gather + permute" if world > 1 else "") + "), y rows -> pinned host"}
+                       + (" storing y into every rank over NVLink" if world > 1 else "") + "), y rows -> pinned host"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -384,7 +386,7 @@ def ours(args: argparse.Namespace) -> None:
             "data": "synthetic (seeded: W ~ N(0, 0.015), x ~ N(0, 1))",
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_COLS, "batch": B, "bits": 4,
                        "group_size": GROUP, "symmetric": True,
-                       "parallelism": f"row-sharded x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "parallelism": f"row-sharded x{world}" + (" + NVLink peer stores of y" if world > 1 else ""),
                        "l2": "working set larger than L2 (x 134 MB, y 470 MB, weights 132 MB at batch 4096); "
                              "sweep lines flush L2 (256 MB write, then a 256 MB read of another buffer) "
                              "between iterations"},
