@@ -386,7 +386,8 @@ def ours(args: argparse.Namespace) -> None:
             "data": "synthetic (seeded: W ~ N(0, 0.015), x ~ N(0, 1))",
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_COLS, "batch": B, "bits": 4,
                        "group_size": GROUP, "symmetric": True,
-                       "parallelism": f"row-sharded x{world}" + (" + NVLink peer stores of y" if world > 1 else ""),
+                       "parallelism": f"row-sharded x{world}" + (f" + y stored into every rank ({lin.exchange})"
+                                                                   if world > 1 else ""),
                        "l2": "working set larger than L2 (x 134 MB, y 470 MB, weights 132 MB at batch 4096); "
                              "sweep lines flush L2 (256 MB write, then a 256 MB read of another buffer) "
                              "between iterations"},

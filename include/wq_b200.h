@@ -220,16 +220,20 @@ WQ_API int wq_ipc_close_handle(void* ptr, int64_t offset);
 
 /* wq_dequant_gemm_f32 with the output written to n_out buffers (1 <= n_out
  * <= WQ_MAX_OUTPUTS, a host array of device pointers, local or peer-mapped),
- * each holding the [B, M] result at row stride ldy. The tensor-core path
- * stores into all of them from its epilogue; the other paths compute into
- * y_out[0] and copy it to the rest on the same stream. */
+ * each holding the [B, M] result at row stride ldy. The decode and
+ * tensor-core kernels store into all of them as they finish each value; the
+ * tiled fallback computes into y_out[0] and copies it to the rest on the same
+ * stream. y_all, when not NULL, is an NVLink-switch address (NVLS) that
+ * reaches the same position in every rank's buffer: the decode and
+ * tensor-core kernels then issue one multimem.st per value instead of n_out
+ * stores, and y_out is used only by the fallback. */
 WQ_API int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
                                      const uint8_t* q, int64_t M, int64_t q_cols,
                                      const float* scales, int64_t scale_rows, int64_t groups,
                                      const float* zeros, int64_t zero_rows, int64_t zero_groups,
                                      const float* channel_scale, int64_t channel_len,
                                      int group_size, int bits,
-                                     float* const* y_out, int n_out, int64_t ldy,
+                                     float* const* y_out, int n_out, int64_t ldy, float* y_all,
                                      void* workspace, size_t workspace_bytes,
                                      void* stream);
 

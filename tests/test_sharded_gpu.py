@@ -72,6 +72,7 @@ def _nccl_worker(rank: int, world: int, port: int, out_dir: str) -> None:
         bits=4, group_size=128, in_features=K, out_features=mp_, symmetric=True, packed=True, granularity="group")
     lin = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="nccl")
     p2p = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="p2p")
+    nvls = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="nvls")
     for b in (1, 64):
         x = torch.randn(b, K, generator=g).to(dev)
         y = lin.forward(x)
@@ -79,9 +80,12 @@ def _nccl_worker(rank: int, world: int, port: int, out_dir: str) -> None:
         for rep in range(2):   # the second call reuses the mapped peer buffers
             y2 = p2p.forward(x)
             np.save(os.path.join(out_dir, f"p2p{rank}_b{b}_{rep}.npy"), y2.cpu().numpy())
+            y3 = nvls.forward(x)
+            np.save(os.path.join(out_dir, f"nvls{rank}_b{b}_{rep}.npy"), y3.cpu().numpy())
     torch.cuda.synchronize()
     dist.barrier()
     p2p.close()
+    nvls.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -104,3 +108,4 @@ def test_row_parallel_nccl_matches_unsharded(wq, cuda, tmp_path) -> None:
             # the peer-store exchange delivers the same values bit for bit
             for rep in range(2):
                 assert np.array_equal(np.load(tmp_path / f"p2p{r}_b{b}_{rep}.npy"), got), (r, b, rep)
+                assert np.array_equal(np.load(tmp_path / f"nvls{r}_b{b}_{rep}.npy"), got), ("nvls", r, b, rep)

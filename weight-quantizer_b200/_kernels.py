@@ -67,7 +67,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
-         _int, _int, _vp, _int, _i64, _vp, _sz, _vp],
+         _int, _int, _vp, _int, _i64, _vp, _vp, _sz, _vp],
     ),
 }
 
@@ -363,11 +363,14 @@ def dequant_gemm_multi(
     bits: int,
     outputs: list[int],
     ldy: int,
+    y_all: int = 0,
 ) -> None:
     """dequant_gemm writing the same [B, M] result (row stride ``ldy``) into
     every device pointer of ``outputs`` (this GPU's buffers or peer buffers
     mapped with :func:`ipc_open`). The first output must be on the inputs'
-    device; the tensor-core path stores into all of them from its epilogue."""
+    device; the tensor-core path stores into all of them from its epilogue.
+    ``y_all`` (nonzero) is an NVLink-switch address that reaches every rank's
+    buffer at once; the tensor-core epilogue then stores through it alone."""
     if x.ndim != 2:
         raise ValueError("x must have shape [B, K]")
     if q.ndim != 2 or scales.ndim != 2 or zeros.ndim != 2:
@@ -397,7 +400,7 @@ def dequant_gemm_multi(
         _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
         _ptr(channel_scale), ch_len,
         int(group_size), int(bits),
-        ctypes.cast(arr, ctypes.c_void_p), len(outputs), int(ldy),
+        ctypes.cast(arr, ctypes.c_void_p), len(outputs), int(ldy), ctypes.c_void_p(int(y_all)) if y_all else None,
         _ptr(ws), ws_bytes,
         _stream(dev),
     )

@@ -141,7 +141,8 @@ namespace {
 int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, int64_t q_cols,
              const float* scales, int64_t scale_rows, int64_t groups, const float* zeros, int64_t zero_rows,
              int64_t zero_groups, const float* channel_scale, int64_t channel_len, int group_size, int bits,
-             float* const* y_out, int n_out, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+             float* const* y_out, int n_out, int64_t ldy, float* y_all, void* workspace, size_t workspace_bytes,
+             void* stream) {
     // dequant_gemm.cpp:241-276, same order
     if (bits != 4 && bits != 8) return WQ_E_BITS;
     if (group_size <= 0) return WQ_E_GROUP_SIZE;
@@ -179,6 +180,7 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
     p.channel = channel_scale;
     p.y = y_out[0];
     p.n_extra = 0;
+    p.y_all = nullptr;
     for (int i = 0; i < 7; ++i) p.y_extra[i] = nullptr;
     p.B = B;
     p.M = M;
@@ -192,17 +194,26 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
 
     cudaError_t e;
     bool copies = n_out > 1;   // paths without a multi-output epilogue copy afterwards
+    // the decode and tensor-core kernels store into every output themselves
+    auto fan_out = [&]() {
+        if (y_all != nullptr) {
+            p.y_all = y_all;
+        } else {
+            p.n_extra = n_out - 1;
+            for (int i = 1; i < n_out; ++i) p.y_extra[i - 1] = y_out[i];
+        }
+        copies = false;
+    };
     if (wq::gemv_supported(p)) {
         const size_t need = wq::gemv_workspace_bytes(B, K, bits);
         if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
+        fan_out();
         e = wq::launch_gemv(p, workspace, s);
     } else if (wq::tc_supported(p)) {
         const size_t need = wq::tc_workspace_bytes(B, K);
         if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
         if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
-        p.n_extra = n_out - 1;
-        for (int i = 1; i < n_out; ++i) p.y_extra[i - 1] = y_out[i];
-        copies = false;
+        fan_out();
         e = wq::launch_tc(p, workspace, s);
     } else {
         e = wq::launch_gemm_simt(p, s);
@@ -248,7 +259,7 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
                         void* stream) {
     float* const outs[1] = {y};
     return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
-                    channel_len, group_size, bits, y == nullptr ? nullptr : outs, 1, ldy, workspace,
+                    channel_len, group_size, bits, y == nullptr ? nullptr : outs, 1, ldy, nullptr, workspace,
                     workspace_bytes, stream);
 }
 
@@ -258,11 +269,11 @@ int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
                               const float* zeros, int64_t zero_rows, int64_t zero_groups,
                               const float* channel_scale, int64_t channel_len,
                               int group_size, int bits,
-                              float* const* y_out, int n_out, int64_t ldy,
+                              float* const* y_out, int n_out, int64_t ldy, float* y_all,
                               void* workspace, size_t workspace_bytes,
                               void* stream) {
     return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
-                    channel_len, group_size, bits, y_out, n_out, ldy, workspace, workspace_bytes, stream);
+                    channel_len, group_size, bits, y_out, n_out, ldy, y_all, workspace, workspace_bytes, stream);
 }
 
 size_t wq_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }

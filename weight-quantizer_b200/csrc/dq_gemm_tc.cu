@@ -65,6 +65,7 @@ struct TcParams {
     float* y;
     float* y_extra[7];    // further outputs with y's layout (peer-mapped on other GPUs)
     int n_extra;
+    float* y_all;         // NVLink-switch address reaching every rank's y, or nullptr
     unsigned int* fault;
     int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
@@ -85,6 +86,11 @@ __device__ __forceinline__ bool elect_one() {
         "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(pred));
     return pred != 0;
+}
+// Store through an NVLink-switch (NVLS) address: the switch writes the value
+// into the same position of every rank's buffer bound to that address.
+__device__ __forceinline__ void st_all_ranks(float* addr, float v) {
+    asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -560,12 +566,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             // travel over NVLink while other tiles still compute. No fence:
             // the kernel's completion makes its peer stores visible to work
             // ordered after it, and the caller orders the ranks after the call.
-            for (int d = 0; d <= p.n_extra; ++d) {
-                float* dst = d == 0 ? p.y : p.y_extra[d - 1];
+            if (p.y_all != nullptr) {
+                // one store reaches every rank's y through the NVLink switch
 #pragma unroll
                 for (int i = 0; i < BN; ++i) {
                     const int n = n0 + i;
-                    if (n < p.B) dst[(int64_t)n * p.ldy + m] = acc[i] * __ldg(p.inv_s + n);
+                    if (n < p.B) st_all_ranks(p.y_all + (int64_t)n * p.ldy + m, acc[i] * __ldg(p.inv_s + n));
+                }
+            } else {
+                for (int d = 0; d <= p.n_extra; ++d) {
+                    float* dst = d == 0 ? p.y : p.y_extra[d - 1];
+#pragma unroll
+                    for (int i = 0; i < BN; ++i) {
+                        const int n = n0 + i;
+                        if (n < p.B) dst[(int64_t)n * p.ldy + m] = acc[i] * __ldg(p.inv_s + n);
+                    }
                 }
             }
         }
@@ -703,6 +718,7 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.inv_s = w.inv_s;
     p.y = g.y;
     p.n_extra = g.n_extra;
+    p.y_all = g.y_all;
     for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;

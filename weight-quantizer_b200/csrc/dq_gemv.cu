@@ -114,6 +114,9 @@ struct GemvParams {
     const float* zeros;
     const float* channel;
     float* y;
+    float* y_extra[7];   // further outputs with y's layout (peer-mapped on other GPUs)
+    int n_extra;
+    float* y_all;        // NVLink-switch address reaching every rank's y, or nullptr
     unsigned int* fault;
     int M, K, NCH;
     int64_t q_stride, ldy;
@@ -392,7 +395,14 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
                     for (int bb = 0; bb < NB; ++bb)
                         if (bb == b) e = eb[bb];
                     const int h = 25 + e, h1 = h / 2;
-                    p.y[(int64_t)b * p.ldy + row] = (v * pow2i(h1)) * pow2i(h - h1);
+                    const float out = (v * pow2i(h1)) * pow2i(h - h1);
+                    const int64_t off = (int64_t)b * p.ldy + row;
+                    if (p.y_all != nullptr) {
+                        asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(p.y_all + off), "f"(out) : "memory");
+                    } else {
+                        p.y[off] = out;
+                        for (int d = 0; d < p.n_extra; ++d) p.y_extra[d][off] = out;
+                    }
                 }
             }
             __syncwarp();
@@ -547,6 +557,9 @@ cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t 
     p.zeros = g.zeros;
     p.channel = g.channel;
     p.y = g.y;
+    p.n_extra = g.n_extra;
+    p.y_all = g.y_all;
+    for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;
     p.M = (int)g.M;

@@ -17,6 +17,7 @@ struct GemmProblem {
     float* y;              // [B, ldy]
     float* y_extra[7];     // further outputs with y's layout (peer-mapped or local)
     int n_extra;           // entries of y_extra in use
+    float* y_all;          // NVLink-switch address reaching every rank's y, or nullptr
     int64_t B, M, K;
     int64_t q_stride;      // bytes per stored row: K (int8) or (K+1)/2 (int4)
     int64_t ldy;

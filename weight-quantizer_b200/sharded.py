@@ -8,11 +8,22 @@ padded with rows whose output is dropped), while x and the channel scale are
 replicated. Per-tensor granularity (one scale for all rows) is replicated on
 every rank. When the whole y is needed on every rank there are two exchanges:
 
-* ``exchange="p2p"`` (default on GPUs): every rank maps the other ranks' full
+* ``exchange="p2p"``: every rank maps the other ranks' full
   y buffers [B, world*Mp] once (CUDA IPC over NVLink) and the dequant-GEMM's
   epilogue stores each finished value into all of them, so the exchange
-  overlaps the computation; one-element NCCL all-reduces before and after the
-  call order the ranks around it.
+  overlaps the computation. y alternates between two buffers, so a
+  one-element NCCL all-reduce after each call is the only ordering needed:
+  when any rank starts call i+2 (which rewrites the buffer of call i), every
+  rank has passed call i+1's all-reduce and therefore finished whatever it
+  did with call i's y before call i+1. A returned y stays valid until the
+  second following forward with the same batch size.
+* ``exchange="nvls"``: the full y buffers are PyTorch symmetric memory and
+  the epilogue stores each value once through the NVLink switch address that
+  reaches every rank's buffer (NVLS), so each GPU sends its rows once instead
+  of once per peer; falls back to peer stores where the switch address is not
+  available. Same ordering as p2p.
+* ``exchange="auto"`` (default): nvls, or p2p if symmetric memory cannot be
+  set up on this system.
 * ``exchange="nccl"``: the kernel writes the local shard, one NCCL all-gather
   collects [world, B, Mp] and a permute kernel lays it out as [B, M].
 """
@@ -76,7 +87,7 @@ class RowParallelDequantLinear:
     """One rank's part of a row-sharded quantized linear layer (no bias)."""
 
     def __init__(self, shard: QuantizedWeight, out_features: int, rank: int, world: int,
-                 group: dist.ProcessGroup | None = None, exchange: str = "p2p") -> None:
+                 group: dist.ProcessGroup | None = None, exchange: str = "auto") -> None:
         mp, _ = shard_rows(out_features, world)
         if shard.out_features != mp:
             raise ValueError("shard height does not match the row split")
@@ -88,12 +99,16 @@ class RowParallelDequantLinear:
         self.world = world
         self.group = group
         self.mp = mp
-        if exchange not in ("p2p", "nccl"):
-            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        if exchange not in ("auto", "p2p", "nvls", "nccl"):
+            raise ValueError("exchange must be 'auto', 'p2p', 'nvls' or 'nccl'")
         self.exchange = exchange
         self._bufs: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
-        # batch -> (full y, output pointers (own first), opened (ptr, offset) list, sync word)
-        self._peer: dict[int, tuple[torch.Tensor, list[int], list[tuple[int, int]], torch.Tensor]] = {}
+        # batch -> two (full y, output pointers (own first), opened (ptr, offset) list) sets
+        self._peer: dict[int, list[tuple[torch.Tensor, list[int], list[tuple[int, int]]]]] = {}
+        # batch -> two (full y, output pointers (own first), switch address or 0, handle) sets
+        self._nvls: dict[int, list[tuple[torch.Tensor, list[int], int, object]]] = {}
+        self._calls: dict[int, int] = {}
+        self._sync: torch.Tensor | None = None
 
     def _buffers(self, batch: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         if batch not in self._bufs:
@@ -109,48 +124,88 @@ class RowParallelDequantLinear:
         s = self.shard
         return _kernels.dequant_gemm(x, s.codes, s.scales, s.zeros, s.channel_scale, s.group_size, s.bits, out=out)
 
-    def _peer_buffers(self, batch: int) -> tuple[torch.Tensor, list[int], list[tuple[int, int]], torch.Tensor]:
-        """Full y [B, world*Mp] on this rank and the pointers at which this
-        rank's columns start in every rank's full y (own buffer first)."""
+    def _sync_word(self) -> torch.Tensor:
+        if self._sync is None:
+            self._sync = torch.zeros(1, dtype=torch.float32, device=self.shard.codes.device)
+        return self._sync
+
+    def _peer_buffers(self, batch: int) -> list[tuple[torch.Tensor, list[int], list[tuple[int, int]]]]:
+        """Two full y [B, world*Mp] buffers on this rank, each with the pointers
+        at which this rank's columns start in every rank's copy (own first)."""
         if batch not in self._peer:
             dev = self.shard.codes.device
-            full = torch.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
-            handle = _kernels.ipc_handle(full)
-            handles: list[tuple[bytes, int] | None] = [None] * self.world
-            dist.all_gather_object(handles, handle, group=self.group)
-            col = self.rank * self.mp * 4
-            outs = [full.data_ptr() + col]
-            opened: list[tuple[int, int]] = []
-            for r in range(self.world):
-                if r == self.rank:
-                    continue
-                h = handles[r]
-                assert h is not None
-                ptr = _kernels.ipc_open(h[0], h[1])
-                opened.append((ptr, h[1]))
-                outs.append(ptr + col)
-            sync = torch.zeros(1, dtype=torch.float32, device=dev)
-            self._peer[batch] = (full, outs, opened, sync)
+            sets = []
+            for _ in range(2):
+                full = torch.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
+                handles: list[tuple[bytes, int] | None] = [None] * self.world
+                dist.all_gather_object(handles, _kernels.ipc_handle(full), group=self.group)
+                col = self.rank * self.mp * 4
+                outs = [full.data_ptr() + col]
+                opened: list[tuple[int, int]] = []
+                for r in range(self.world):
+                    if r == self.rank:
+                        continue
+                    h = handles[r]
+                    assert h is not None
+                    ptr = _kernels.ipc_open(h[0], h[1])
+                    opened.append((ptr, h[1]))
+                    outs.append(ptr + col)
+                sets.append((full, outs, opened))
+            self._peer[batch] = sets
         return self._peer[batch]
+
+    def _nvls_buffers(self, batch: int) -> list[tuple[torch.Tensor, list[int], int, object]]:
+        """Two full y buffers in symmetric memory, with this rank's column
+        pointers in every rank's copy and the NVLink-switch address (0 when the
+        system has none)."""
+        if batch not in self._nvls:
+            from torch.distributed import _symmetric_memory as symm_mem
+
+            dev = self.shard.codes.device
+            group = self.group if self.group is not None else dist.group.WORLD
+            col = self.rank * self.mp * 4
+            sets = []
+            for _ in range(2):
+                full = symm_mem.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
+                handle = symm_mem.rendezvous(full, group)
+                ptrs = [int(p) for p in handle.buffer_ptrs]
+                outs = [ptrs[self.rank] + col] + [ptrs[r] + col for r in range(self.world) if r != self.rank]
+                switch = int(getattr(handle, "multicast_ptr", 0) or 0)
+                sets.append((full, outs, switch + col if switch else 0, handle))
+            self._nvls[batch] = sets
+        return self._nvls[batch]
 
     def close(self) -> None:
         """Unmaps the peers' y buffers (every rank calls it; the mappings also
         end with the process)."""
-        for _, _, opened, _ in self._peer.values():
-            for ptr, off in opened:
-                _kernels.ipc_close(ptr, off)
+        for sets in self._peer.values():
+            for _, _, opened in sets:
+                for ptr, off in opened:
+                    _kernels.ipc_close(ptr, off)
         self._peer.clear()
+        self._nvls.clear()
 
     def forward(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
         """y [B, M] on every rank (gather=True), else this rank's [B, Mp] shard."""
         batch = int(x.shape[0])
-        if gather and self.world > 1 and self.exchange == "p2p":
-            full, outs, _, sync = self._peer_buffers(batch)
+        if gather and self.world > 1 and self.exchange == "auto":
+            try:
+                self._nvls_buffers(batch)
+                self.exchange = "nvls"
+            except (RuntimeError, AttributeError, ImportError):
+                self.exchange = "p2p"
+        if gather and self.world > 1 and self.exchange in ("nvls", "p2p"):
+            k = self._calls.get(batch, 0)
+            self._calls[batch] = k + 1
             s = self.shard
-            dist.all_reduce(sync, group=self.group)   # every rank is done with its previous y
+            if self.exchange == "nvls":
+                full, outs, switch, _ = self._nvls_buffers(batch)[k & 1]
+            else:
+                full, outs, _ = self._peer_buffers(batch)[k & 1]
+                switch = 0
             _kernels.dequant_gemm_multi(x, s.codes, s.scales, s.zeros, s.channel_scale, s.group_size, s.bits,
-                                        outs, self.world * self.mp)
-            dist.all_reduce(sync, group=self.group)   # every rank's rows have landed in every y
+                                        outs, self.world * self.mp, y_all=switch)
+            dist.all_reduce(self._sync_word(), group=self.group)   # every rank's rows are in every y
             return full[:, : self.out_features]
         local, gathered, full = self._buffers(batch)
         self.forward_local(x, out=local)
