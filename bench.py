@@ -343,15 +343,23 @@ def ours(args: argparse.Namespace) -> None:
     # ---- end to end through the public API with pinned host buffers --------
     e2e = None
     if not args.no_e2e:
-        x_h = layer.x[B].pin_memory()
+        # Each rank brings 1/N of the batch rows in from pinned host memory and
+        # takes 1/N of the output rows back; for N > 1 an NCCL all-gather
+        # assembles the whole x on every rank over NVLink.
         rows_per_rank = (B + world - 1) // world
         b0, b1 = min(rank * rows_per_rank, B), min((rank + 1) * rows_per_rank, B)
+        x_h = torch.zeros((rows_per_rank, K_COLS), dtype=torch.float32)
+        x_h[: b1 - b0] = layer.x[B][b0:b1]
+        x_h = x_h.pin_memory()
         y_h = torch.empty((b1 - b0, M_ROWS), dtype=torch.float32).pin_memory()
-        x_d = torch.empty_like(x)
+        x_all = torch.empty((world * rows_per_rank, K_COLS), dtype=torch.float32, device=dev)
+        x_mine = x_all[rank * rows_per_rank:(rank + 1) * rows_per_rank]
 
         def e2e_step() -> None:
-            x_d.copy_(x_h, non_blocking=True)
-            y = lin.forward(x_d)
+            x_mine.copy_(x_h, non_blocking=True)
+            if world > 1:
+                dist.all_gather_into_tensor(x_all, x_mine)
+            y = lin.forward(x_all[:B])
             y_h.copy_(y[b0:b1], non_blocking=True)
 
         for _ in range(args.warmup):
@@ -367,10 +375,14 @@ def ours(args: argparse.Namespace) -> None:
         barrier()
         t_e2e = max_over_ranks(s0.elapsed_time(s1) / args.steps / 1e3)
         e2e = {"value": round(flops / t_e2e / 1e9, 1), "unit": "GFLOP/s",
-               "h2d_bytes_per_step": int(world * B * K_COLS * 4), "d2h_bytes_per_step": int(B * M_ROWS * 4),
+               "h2d_bytes_per_step": int(world * rows_per_rank * K_COLS * 4),
+               "d2h_bytes_per_step": int(B * M_ROWS * 4),
                "ms_per_step": round(t_e2e * 1e3, 3),
-               "path": "pinned x -> device, RowParallelDequantLinear.forward (dequant_gemm kernel"
-                       + (" storing y into every rank over NVLink" if world > 1 else "") + "), y rows -> pinned host"}
+               "path": "each rank: its 1/N of x rows pinned host -> device"
+                       + (", NCCL all-gather of x" if world > 1 else "")
+                       + ", RowParallelDequantLinear.forward (dequant_gemm kernel"
+                       + (" storing y into every rank over NVLink" if world > 1 else "")
+                       + "), its 1/N of y rows -> pinned host"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
