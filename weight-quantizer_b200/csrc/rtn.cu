@@ -236,6 +236,85 @@ __global__ void __launch_bounds__(kRtnWarps * 32) rtn_rows_kernel(const RtnProbl
     }
 }
 
+// Group kernel for the common layout: K % G == 0, G in {8, ..., 256} (a power
+// of two), K % 8 == 0. The matrix is walked as a flat sequence of 8-element
+// chunks in row-major order; LPG = G / 8 consecutive lanes hold one group, a
+// warp step covers 256 elements (whole groups, possibly of two rows). Each
+// lane loads its chunk with two 16-byte loads, the group's statistics are
+// exact shuffle reductions over its LPG lanes, and each lane packs its 8 codes
+// into one 32-bit (int4) or 64-bit (int8) store. Same operations per element
+// as rtn_rows_kernel, so the outputs are identical.
+template <int LPG>
+__global__ void __launch_bounds__(256) rtn_groups_kernel(const RtnProblem p) {
+    const int lane = threadIdx.x & 31;
+    const int qmax = (1 << p.bits) - 1;
+    const int64_t G = (int64_t)LPG * 8;
+    const int64_t groups = p.K / G;
+    const int64_t chunks_per_row = p.K / 8;
+    const int64_t total = p.M * chunks_per_row;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    bool bad = false;
+    for (int64_t base = warp0 * 32; base < total; base += nwarps * 32) {
+        const int64_t c = base + lane;
+        const bool live = c < total;
+        const int64_t row = live ? c / chunks_per_row : 0;
+        const int64_t k = live ? (c - row * chunks_per_row) * 8 : 0;
+        float v[8];
+        Stats st;
+        stats_init(st);
+        if (live) {
+            const float4 a = *reinterpret_cast<const float4*>(p.w + row * p.K + k);
+            const float4 b = *reinterpret_cast<const float4*>(p.w + row * p.K + k + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (!isfinite(v[i])) bad = true;
+            if (p.pre_scale != nullptr) {
+                const float4 sa = *reinterpret_cast<const float4*>(p.pre_scale + k);
+                const float4 sb = *reinterpret_cast<const float4*>(p.pre_scale + k + 4);
+                const float sc[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], sc[i]);
+            }
+            const unsigned long long pos0 = (unsigned long long)(k % G);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) stats_add(st, v[i], pos0 + i);
+        }
+        // exact statistics of the group held by LPG consecutive lanes
+#pragma unroll
+        for (int o = LPG / 2; o > 0; o >>= 1) {
+            Stats t;
+            t.amax = __shfl_xor_sync(0xffffffffu, st.amax, o);
+            t.vmin = __shfl_xor_sync(0xffffffffu, st.vmin, o);
+            t.vmax = __shfl_xor_sync(0xffffffffu, st.vmax, o);
+            t.zkey = __shfl_xor_sync(0xffffffffu, st.zkey, o);
+            stats_merge(st, t);
+        }
+        if (!live) continue;
+        float scale, zero;
+        qparams(st, p.symmetric, qmax, scale, zero);
+        if ((lane & (LPG - 1)) == 0) {
+            p.scales_out[row * groups + k / G] = scale;
+            p.zeros_out[row * groups + k / G] = zero;
+        }
+        uint32_t cd[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cd[i] = code_of(v[i], scale, zero, qmax);
+        if (p.bits == 4) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) word |= (cd[i] & 0xFu) << (4 * i);
+            *reinterpret_cast<uint32_t*>(p.q_out + row * (p.K / 2) + k / 2) = word;
+        } else {
+            const uint2 w2 = make_uint2(cd[0] | (cd[1] << 8) | (cd[2] << 16) | (cd[3] << 24),
+                                        cd[4] | (cd[5] << 8) | (cd[6] << 16) | (cd[7] << 24));
+            *reinterpret_cast<uint2*>(p.q_out + row * p.K + k) = w2;
+        }
+    }
+    if (bad) atomicOr(p.flags, 1);
+}
+
 __global__ void minmax_init_kernel(int32_t* mm) {
     mm[0] = INT_MAX;
     mm[1] = INT_MIN;
@@ -344,6 +423,24 @@ cudaError_t launch_rtn(const RtnProblem& p, void* workspace, cudaStream_t s) {
         n_partial = kTensorBlocks;
         tensor_stats_kernel<<<kTensorBlocks, 256, 0, s>>>(p, partial);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    const int64_t G = p.group_mode;
+    const bool aligned = (reinterpret_cast<uintptr_t>(p.w) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.q_out) & 7) == 0 &&
+                         (p.pre_scale == nullptr || (reinterpret_cast<uintptr_t>(p.pre_scale) & 15) == 0);
+    if (G >= 8 && G <= 256 && (G & (G - 1)) == 0 && p.K % G == 0 && aligned) {
+        const int64_t warps_needed = (p.M * (p.K / 8) + 31) / 32;
+        int64_t blocks = (warps_needed + 7) / 8;
+        const int64_t cap = (int64_t)sm_count() * 8;
+        if (blocks > cap) blocks = cap;
+        switch (G) {
+            case 8: rtn_groups_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+            case 16: rtn_groups_kernel<2><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+            case 32: rtn_groups_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+            case 64: rtn_groups_kernel<8><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+            case 128: rtn_groups_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+            default: rtn_groups_kernel<32><<<(unsigned)blocks, 256, 0, s>>>(p); break;
+        }
+        return cudaGetLastError();
     }
     int warps = kRtnWarps;
     const int64_t smem_cap = 200 * 1024;
