@@ -51,9 +51,16 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int kThreads = 384;    // 12 warps
+constexpr int kThreads = 512;    // 16 warps = 4 warpgroups
 constexpr int kBand = 16;        // batch tiles per rasterization band
-constexpr int kWarpB = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 6, kWarpCodes = 10, kWarpSched = 11;
+// warpgroup 0: producers, MMA issuer, scheduler; 1 and 2: dequant (K tile 0
+// and 1 of every A stage); 3: epilogue
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpCodes = 2, kWarpSched = 3, kWarpDq0 = 4, kWarpEpi0 = 12;
+constexpr int kDqWarps = 8;
+// Registers per thread after the warpgroups re-split the launch's 128 (the
+// sum, times 128 threads each, must not exceed 512 x 128).
+constexpr int kRegsCtl = 40, kRegsDq = 112, kRegsEpi = 232;
+static_assert(kRegsCtl + 2 * kRegsDq + kRegsEpi <= 4 * 128, "register split exceeds the launch's registers");
 constexpr int kCodeRowBytes = 128;  // packed code bytes per row per codes stage
 constexpr int kNC = 2;              // codes stages
 
@@ -130,6 +137,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -246,12 +266,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < NA; ++s) {
-            mbar_init(full_a(s), 4);      // one arrival per dequant warp
+            mbar_init(full_a(s), kDqWarps);   // one arrival per dequant warp
             mbar_init(empty_a(s), 1);
         }
         for (int c = 0; c < kNC; ++c) {
             mbar_init(c_full(c), 1);
-            mbar_init(c_empty(c), 4);     // one arrival per dequant warp
+            mbar_init(c_empty(c), kDqWarps);  // one arrival per dequant warp
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
@@ -297,7 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     };
 
-    if (warp == kWarpB) {
+    // Each warpgroup re-splits the registers on entering its role: the
+    // control warps need few, the epilogue holds BN fp32 accumulators per
+    // thread. setmaxnreg is warpgroup-wide, so warpgroup 0 issues it before
+    // its warps branch into their roles.
+    if (warp < kWarpDq0) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+      if (warp == kWarpB) {
         // x' planes: one bulk copy of both planes of a K tile per stage
         if (lane == 0) {
             const uint32_t tile_bytes = (uint32_t)L::STAGE;
@@ -316,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             drain(NS, p.KT, full_b);
         }
-    } else if (warp == kWarpCodes) {
+      } else if (warp == kWarpCodes) {
         // packed codes: KC K tiles per 2D box (128 rows x 128 bytes, 128-byte
         // swizzle so that the dequant threads read them without bank conflicts)
         if (lane == 0) {
@@ -334,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             drain(kNC, nct, c_full);
         }
-    } else if (warp == kWarpSched) {
+      } else if (warp == kWarpSched) {
         // Scheduler: walks the tiles in order, waits for each tile's x' stage,
         // A stage (first tile of a stage) and accumulator (first tile of a
         // group), and publishes how many tiles are ready. The MMA thread reads
@@ -370,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp == kWarpMma) {
+      } else {
         // One thread issues every MMA: it reads the scheduler's ready count,
         // then issues every ready tile (up to kIssueBatch) back to back.
         // A comes from tensor memory; B descriptors are built once and a
@@ -431,10 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             drain(NS, p.KT, empty_b);
             drain(NA, n_astages, empty_a);
         }
+      }
     } else if (warp < kWarpEpi0) {
-        // ---- dequant: warp w writes TMEM lanes 32 (w % 4) .. + 31, thread =
-        // one weight row; each A stage holds two K tiles ---------------------
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDq));
+        // ---- dequant: warp w writes TMEM lanes 32 (w % 4) .. + 31 (thread =
+        // one weight row) for K tile `half` of every A stage; the other
+        // warpgroup writes the stage's other K tile ----------------------------
         const int q = warp & 3;
+        const int half = (warp - kWarpDq0) >> 2;
         const int r = q * 32 + lane;
         const int64_t m = min(m0 + r, p.M - 1);
         const int64_t srow = p.scale_rows == 1 ? 0 : m;
@@ -450,81 +480,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         float z_n2 = p.ngroups > 2 ? __ldg(zrow + 2) : 0.0f;
         float z_n3 = p.ngroups > 3 ? __ldg(zrow + 3) : 0.0f;
         float z_n4 = p.ngroups > 4 ? __ldg(zrow + 4) : 0.0f;
-        int sa = 0, c = 0, kin = 0, gin = 0, g = 0;
+        int g = 0, gin = half;   // this warp's tile t = 2 ja + half is tile gin of group g
+        auto next_group = [&]() {
+            gin -= p.ktg;
+            ++g;
+            z_cur = z_n1;
+            z_n1 = z_n2;
+            z_n2 = z_n3;
+            z_n3 = z_n4;
+            if (g + 4 < p.ngroups) z_n4 = __ldg(zrow + g + 4);
+        };
+        while (gin >= p.ktg) next_group();
+        const int nct = (p.KT + L::KC - 1) / L::KC;
+        int sa = 0, c = 0, ja = 0;
         uint32_t pha = 0, cph = 0;
-        int t = 0;
-        for (int ja = 0; ja < n_astages; ++ja) {
-            if (ja >= NA) wait_warp(empty_a(sa), pha ^ 1u);
-            tc_fence_after();
-            const uint32_t a_stage = tmem_a0 + lane_base + (uint32_t)(sa * kAStageCols);
-            for (int h = 0; h < kTilesPerA && t < p.KT; ++h, ++t) {
-                if (gin == p.ktg) {   // next group: rotate the prefetched zero points
-                    gin = 0;
-                    ++g;
-                    z_cur = z_n1;
-                    z_n1 = z_n2;
-                    z_n2 = z_n3;
-                    z_n3 = z_n4;
-                    if (g + 4 < p.ngroups) z_n4 = __ldg(zrow + g + 4);
+        for (int ct = 0; ct < nct; ++ct) {
+            wait_warp(c_full(c), cph);
+            const unsigned char* crow = smem + L::C_OFF + c * L::C_STAGE + r * kCodeRowBytes;
+            for (int js = 0; js < L::KC / kTilesPerA && ja < n_astages; ++js, ++ja) {
+                if (ja >= NA) wait_warp(empty_a(sa), pha ^ 1u);
+                tc_fence_after();
+                const int t = kTilesPerA * ja + half;
+                if (t < p.KT) {
+                    const int kin = kTilesPerA * js + half;   // K tile inside the codes stage
+                    const float z = z_cur;
+                    const float zb = 1024.0f + z;
+                    const __half zh = __float2half_rn(zb);
+                    if (__half2float(zh) != zb || !(z >= 0.0f && z <= 1023.0f)) inexact = true;
+                    const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
+                    uint32_t a[32];
+                    if constexpr (BITS == 4) {
+                        // K tile = 16-byte chunks 2 kin, 2 kin + 1 of the row (swizzled)
+                        const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin) ^ swz) << 4));
+                        const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin + 1) ^ swz) << 4));
+                        const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const uint4 v = dq8_int4(w[cc], zz);
+                            a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
+                        }
+                    } else {
+                        uint32_t w[16];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(4 * kin + i) ^ swz) << 4));
+                            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+                        }
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const uint4 v = dq8_int8(w[2 * cc], w[2 * cc + 1], zz);
+                            a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
+                        }
+                    }
+                    tmem_st32(tmem_a0 + lane_base + (uint32_t)(sa * kAStageCols + half * (BK / 2)), a);
+                    tmem_wait_st();
                 }
-                const float z = z_cur;
-                const float zb = 1024.0f + z;
-                const __half zh = __float2half_rn(zb);
-                if (__half2float(zh) != zb || !(z >= 0.0f && z <= 1023.0f)) inexact = true;
-                const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
-                if (kin == 0) wait_warp(c_full(c), cph);
-                const unsigned char* crow = smem + L::C_OFF + c * L::C_STAGE + r * kCodeRowBytes;
-                uint32_t a[32];
-                if constexpr (BITS == 4) {
-                    // K tile = 16-byte chunks 2 kin, 2 kin + 1 of the row (swizzled)
-                    const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin) ^ swz) << 4));
-                    const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(2 * kin + 1) ^ swz) << 4));
-                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) {
-                        const uint4 v = dq8_int4(w[cc], zz);
-                        a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
-                    }
-                } else {
-                    uint32_t w[16];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(crow + (((uint32_t)(4 * kin + i) ^ swz) << 4));
-                        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-                    }
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) {
-                        const uint4 v = dq8_int8(w[2 * cc], w[2 * cc + 1], zz);
-                        a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
-                    }
-                }
-                tmem_st32(a_stage + (uint32_t)(h * (BK / 2)), a);
-                ++gin;
-                if (++kin == L::KC || t == p.KT - 1) {
-                    // every code of this codes stage has been consumed (the
-                    // values reached tcgen05.st); the proxy fence orders the
-                    // reads before the TMA unit refills the stage
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(c_empty(c));
-                    kin = 0;
-                    if (++c == kNC) {
-                        c = 0;
-                        cph ^= 1u;
-                    }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full_a(sa));
+                gin += kTilesPerA;   // this warp's next tile is kTilesPerA tiles further on
+                while (gin >= p.ktg) next_group();
+                if (++sa == NA) {
+                    sa = 0;
+                    pha ^= 1u;
                 }
             }
-            tmem_wait_st();
-            tc_fence_before();
+            // every code this warp read from the stage has reached tcgen05.st;
+            // the proxy fence orders the reads before the TMA unit refills it
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(full_a(sa));
-            if (++sa == NA) {
-                sa = 0;
-                pha ^= 1u;
+            if (lane == 0) mbar_arrive(c_empty(c));
+            if (++c == kNC) {
+                c = 0;
+                cph ^= 1u;
             }
         }
         if (inexact) atomicOr(p.fault, 2u);
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
         // ---- epilogue: thread owns row r of the tile, all BN columns -----------
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
@@ -545,12 +578,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             wait_warp(acc_full(buf), (uint32_t)(use & 1));
             tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+            if constexpr (BN > 128) {
+                // 16 columns per load: BN accumulators plus the loaded chunk
+                // stay inside the epilogue's register budget
 #pragma unroll
-            for (int cc = 0; cc < BN / 32; ++cc) {
-                float v[32];
-                tmem_ld32(taddr + 32u * cc, v);
+                for (int cc = 0; cc < BN / 16; ++cc) {
+                    float v[16];
+                    tmem_ld16(taddr + 16u * cc, v);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
+                    for (int i = 0; i < 16; ++i) acc[cc * 16 + i] = fmaf(sc, v[i], acc[cc * 16 + i]);
+                }
+            } else {
+#pragma unroll
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    float v[32];
+                    tmem_ld32(taddr + 32u * cc, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -688,7 +733,11 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint6
 }
 
 int64_t kt_of(int64_t K) { return (K + BK - 1) / BK; }
-int bn_of(int64_t B) { return B <= 32 ? 32 : (B <= 64 ? 64 : 128); }
+// Batch tile: N = 192 for large batches (each MMA then carries 1.5x the work
+// of N = 128 for the same issue cost, with the accumulators still
+// double-buffered in tensor memory), else the smallest of 32/64/128 that
+// covers the batch.
+int bn_of(int64_t B) { return B <= 32 ? 32 : (B <= 64 ? 64 : (B < 1024 ? 128 : 192)); }
 int64_t bpad_of(int64_t B) { const int bn = bn_of(B); return (B + bn - 1) / bn * bn; }
 
 struct TcWorkspace {
@@ -770,11 +819,13 @@ cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
     if (g.bits == 4) {
         if (bn == 32) return launch_bn<32, 12, 4>(g, w, s);
         if (bn == 64) return launch_bn<64, 12, 4>(g, w, s);
-        return launch_bn<128, 6, 4>(g, w, s);
+        if (bn == 128) return launch_bn<128, 6, 4>(g, w, s);
+        return launch_bn<192, 4, 4>(g, w, s);
     }
     if (bn == 32) return launch_bn<32, 12, 8>(g, w, s);
     if (bn == 64) return launch_bn<64, 12, 8>(g, w, s);
-    return launch_bn<128, 6, 8>(g, w, s);
+    if (bn == 128) return launch_bn<128, 6, 8>(g, w, s);
+    return launch_bn<192, 4, 8>(g, w, s);
 }
 
 }  // namespace wq
