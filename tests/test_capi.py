@@ -89,6 +89,30 @@ def test_validation_order_and_codes(wq) -> None:
     assert _call(wq, scale_rows=1, zero_rows=1) == 11
 
 
+def test_multi_output_and_ipc_validation(wq) -> None:
+    """The multi-output entry point runs the same validation as the single-output
+    one, then checks the output count; the IPC calls reject null arguments."""
+    lib = wq._kernels.library()
+
+    def multi(n_out: int, outs=None, bits: int = 4, group_size: int = 8):  # type: ignore[no-untyped-def]
+        return lib.wq_dequant_gemm_f32_multi(None, 1, 8, None, 2, 4, None, 2, 1, None, 2, 1, None, -1,
+                                             group_size, bits, outs, n_out, 2, None, None, 0, None)
+
+    assert multi(1, bits=3) == 3            # reference validation first
+    assert multi(0) == 22                   # WQ_E_OUTPUTS
+    assert multi(9) == 22
+    assert multi(2) == 11                   # null output array
+    arr = (ctypes.c_void_p * 2)(None, None)
+    assert multi(2, outs=ctypes.cast(arr, ctypes.c_void_p)) == 11
+    assert lib.wq_status_string(22).decode() == "output count must be between 1 and WQ_MAX_OUTPUTS"
+    assert lib.wq_ipc_handle_bytes() == 64
+    off = ctypes.c_int64(0)
+    assert lib.wq_ipc_get_handle(None, None, ctypes.byref(off)) == 11
+    ptr = ctypes.c_void_p(0)
+    assert lib.wq_ipc_open_handle(None, 0, ctypes.byref(ptr)) == 11
+    assert lib.wq_ipc_close_handle(None, 0) == 11
+
+
 def test_rtn_and_pack_validation(wq) -> None:
     lib = wq._kernels.library()
     assert lib.wq_rtn_quantize_f32(None, None, 4, 4, 5, 1, 2, None, None, None, None, None, None, 0, None) == 3
