@@ -51,16 +51,46 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int kThreads = 512;    // 16 warps = 4 warpgroups
 constexpr int kBand = 16;        // batch tiles per rasterization band
-// warpgroup 0: producers, MMA issuer, scheduler; 1 and 2: dequant (K tile 0
-// and 1 of every A stage); 3: epilogue
-constexpr int kWarpB = 0, kWarpMma = 1, kWarpCodes = 2, kWarpSched = 3, kWarpDq0 = 4, kWarpEpi0 = 12;
-constexpr int kDqWarps = 8;
-// Registers per thread after the warpgroups re-split the launch's 128 (the
-// sum, times 128 threads each, must not exceed 512 x 128).
-constexpr int kRegsCtl = 40, kRegsDq = 112, kRegsEpi = 232;
-static_assert(kRegsCtl + 2 * kRegsDq + kRegsEpi <= 4 * 128, "register split exceeds the launch's registers");
+// warpgroup 0: producers, MMA issuer, scheduler; then the dequant warpgroups;
+// the last warpgroup runs the epilogue
+constexpr int kWarpB = 0, kWarpMma = 1, kWarpCodes = 2, kWarpSched = 3, kWarpDq0 = 4;
+
+// setmaxnreg toward N registers per thread: .dec only lowers and .inc only
+// raises the count (the other direction is an illegal instruction), so the
+// direction follows from the launch's count.
+template <int N, int LAUNCH>
+__device__ __forceinline__ void set_regs() {
+    if constexpr (N < LAUNCH) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+    } else if constexpr (N > LAUNCH) {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+    }
+}
+
+// Launch shape per batch tile. Wide tiles (BN >= 128): two dequant
+// warpgroups (each writes one K tile of every A stage), one CTA per SM with
+// all 512 columns of tensor memory. Narrow tiles: one dequant warpgroup, two
+// CTAs per SM (half the tensor memory each) so that one CTA's hand-off
+// latency overlaps the other's work. After entering their roles the
+// warpgroups re-split the launch's registers with setmaxnreg; the split must
+// not exceed the launch's registers (checked here and, for the per-thread
+// count ptxas chose, again before the launch).
+template <int BN>
+struct Cfg {
+    static constexpr int DQG = BN >= 128 ? 2 : 1;          // dequant warpgroups
+    static constexpr int THREADS = (2 + DQG) * 128;
+    static constexpr int WARP_EPI0 = kWarpDq0 + 4 * DQG;
+    static constexpr int DQ_WARPS = 4 * DQG;
+    static constexpr int MINB = BN >= 128 ? 1 : 2;        // CTAs per SM
+    static constexpr uint32_t TMEM_COLS = BN >= 128 ? 512 : 256;
+    static constexpr int LAUNCH_REGS = (65536 / (THREADS * MINB)) / 8 * 8;
+    static constexpr int REGS_CTL = 40;
+    static constexpr int REGS_DQ = BN >= 128 ? 112 : 88;
+    static constexpr int REGS_EPI = BN >= 128 ? 232 : 112;
+    static_assert(REGS_CTL + DQG * REGS_DQ + REGS_EPI <= (2 + DQG) * LAUNCH_REGS,
+                  "register split exceeds the launch's registers");
+};
 constexpr int kCodeRowBytes = 128;  // packed code bytes per row per codes stage
 constexpr int kNC = 2;              // codes stages
 
@@ -203,7 +233,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
 // Tensor memory: 512 columns. Columns [0, 2 BN) hold the two group
 // accumulators; the rest is a ring of A stages, each two K tiles wide
 // (2 x 32 columns of packed fp16 pairs, one row per lane).
-constexpr uint32_t kTmemCols = 512;
 constexpr int kTilesPerA = 2;
 constexpr int kAStageCols = kTilesPerA * BK / 2;
 
@@ -211,7 +240,7 @@ template <int BN, int NS, int BITS>
 struct Smem {
     static constexpr int CB = BITS == 4 ? 32 : 64;        // packed code bytes per row per K tile
     static constexpr int KC = kCodeRowBytes / CB;          // K tiles per codes stage
-    static constexpr int NA = (int)(kTmemCols - 2 * BN) / kAStageCols;   // A stages in tensor memory
+    static constexpr int NA = (int)(Cfg<BN>::TMEM_COLS - 2 * BN) / kAStageCols;   // A stages in tensor memory
     static constexpr int B_BYTES = BN * 128;               // one plane of one K tile
     static constexpr int STAGE = 2 * B_BYTES;              // hi + lo planes
     static constexpr int C_STAGE = BM * kCodeRowBytes;
@@ -230,10 +259,13 @@ struct Smem {
 };
 
 template <int BN, int NS, int BITS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     dq_gemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap map_q) {
     using L = Smem<BN, NS, BITS>;
+    using C = Cfg<BN>;
     constexpr int NA = L::NA;
+    constexpr int kWarpEpi0 = C::WARP_EPI0;
+    constexpr uint32_t kTmemCols = C::TMEM_COLS;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // the swizzled tiles need 1024-byte alignment of the dynamic window
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -266,12 +298,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < NA; ++s) {
-            mbar_init(full_a(s), kDqWarps);   // one arrival per dequant warp
+            mbar_init(full_a(s), C::DQ_WARPS);   // one arrival per dequant warp
             mbar_init(empty_a(s), 1);
         }
         for (int c = 0; c < kNC; ++c) {
             mbar_init(c_full(c), 1);
-            mbar_init(c_empty(c), kDqWarps);  // one arrival per dequant warp
+            mbar_init(c_empty(c), C::DQ_WARPS);  // one arrival per dequant warp
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
@@ -322,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // thread. setmaxnreg is warpgroup-wide, so warpgroup 0 issues it before
     // its warps branch into their roles.
     if (warp < kWarpDq0) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+      set_regs<C::REGS_CTL, C::LAUNCH_REGS>();
       if (warp == kWarpB) {
         // x' planes: one bulk copy of both planes of a K tile per stage
         if (lane == 0) {
@@ -459,12 +491,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (warp < kWarpEpi0) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDq));
+        set_regs<C::REGS_DQ, C::LAUNCH_REGS>();
         // ---- dequant: warp w writes TMEM lanes 32 (w % 4) .. + 31 (thread =
-        // one weight row) for K tile `half` of every A stage; the other
-        // warpgroup writes the stage's other K tile ----------------------------
+        // one weight row) for its K tiles of every A stage --------------------
         const int q = warp & 3;
-        const int half = (warp - kWarpDq0) >> 2;
+        // with two dequant warpgroups each writes one K tile of an A stage,
+        // with one it writes both
+        const int h_begin = C::DQG == 2 ? (warp - kWarpDq0) >> 2 : 0;
+        const int h_end = C::DQG == 2 ? h_begin + 1 : kTilesPerA;
         const int r = q * 32 + lane;
         const int64_t m = min(m0 + r, p.M - 1);
         const int64_t srow = p.scale_rows == 1 ? 0 : m;
@@ -480,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float z_n2 = p.ngroups > 2 ? __ldg(zrow + 2) : 0.0f;
         float z_n3 = p.ngroups > 3 ? __ldg(zrow + 3) : 0.0f;
         float z_n4 = p.ngroups > 4 ? __ldg(zrow + 4) : 0.0f;
-        int g = 0, gin = half;   // this warp's tile t = 2 ja + half is tile gin of group g
+        int g = 0, gin = h_begin;   // this warp's next tile t = 2 ja + h is tile gin of group g
         auto next_group = [&]() {
             gin -= p.ktg;
             ++g;
@@ -500,9 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int js = 0; js < L::KC / kTilesPerA && ja < n_astages; ++js, ++ja) {
                 if (ja >= NA) wait_warp(empty_a(sa), pha ^ 1u);
                 tc_fence_after();
-                const int t = kTilesPerA * ja + half;
-                if (t < p.KT) {
-                    const int kin = kTilesPerA * js + half;   // K tile inside the codes stage
+                for (int h = h_begin; h < h_end; ++h) {
+                  const int t = kTilesPerA * ja + h;
+                  if (t < p.KT) {
+                    const int kin = kTilesPerA * js + h;   // K tile inside the codes stage
                     const float z = z_cur;
                     const float zb = 1024.0f + z;
                     const __half zh = __float2half_rn(zb);
@@ -532,13 +567,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                             a[4 * cc] = v.x; a[4 * cc + 1] = v.y; a[4 * cc + 2] = v.z; a[4 * cc + 3] = v.w;
                         }
                     }
-                    tmem_st32(tmem_a0 + lane_base + (uint32_t)(sa * kAStageCols + half * (BK / 2)), a);
-                    tmem_wait_st();
+                    tmem_st32(tmem_a0 + lane_base + (uint32_t)(sa * kAStageCols + h * (BK / 2)), a);
+                  }
+                  if (h + 1 < h_end) {   // the next tile of the same A stage
+                    ++gin;
+                    while (gin >= p.ktg) next_group();
+                  }
                 }
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_a(sa));
-                gin += kTilesPerA;   // this warp's next tile is kTilesPerA tiles further on
+                gin += kTilesPerA - (h_end - 1 - h_begin);   // on to this warp's first tile of the next stage
                 while (gin >= p.ktg) next_group();
                 if (++sa == NA) {
                     sa = 0;
@@ -557,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (inexact) atomicOr(p.fault, 2u);
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
+        set_regs<C::REGS_EPI, C::LAUNCH_REGS>();
         // ---- epilogue: thread owns row r of the tile, all BN columns -----------
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
@@ -785,9 +825,16 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     auto kern = dq_gemm_tc_kernel<BN, NS, BITS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    // the setmaxnreg split assumes the launch gives every thread exactly
+    // LAUNCH_REGS registers; refuse to launch otherwise (the increase would wait
+    // for registers that do not exist)
+    cudaFuncAttributes attr;
+    e = cudaFuncGetAttributes(&attr, kern);
+    if (e != cudaSuccess) return e;
+    if (attr.numRegs != Cfg<BN>::LAUNCH_REGS) return cudaErrorInvalidConfiguration;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    kern<<<(unsigned)grid, kThreads, smem, s>>>(p, mq);
+    kern<<<(unsigned)grid, Cfg<BN>::THREADS, smem, s>>>(p, mq);
     return cudaGetLastError();
 }
 
@@ -817,13 +864,13 @@ cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     // x' stage counts: 192 KB of planes next to two 16 KB codes stages
     if (g.bits == 4) {
-        if (bn == 32) return launch_bn<32, 12, 4>(g, w, s);
-        if (bn == 64) return launch_bn<64, 12, 4>(g, w, s);
+        if (bn == 32) return launch_bn<32, 4, 4>(g, w, s);
+        if (bn == 64) return launch_bn<64, 4, 4>(g, w, s);
         if (bn == 128) return launch_bn<128, 6, 4>(g, w, s);
         return launch_bn<192, 4, 4>(g, w, s);
     }
-    if (bn == 32) return launch_bn<32, 12, 8>(g, w, s);
-    if (bn == 64) return launch_bn<64, 12, 8>(g, w, s);
+    if (bn == 32) return launch_bn<32, 4, 8>(g, w, s);
+    if (bn == 64) return launch_bn<64, 4, 8>(g, w, s);
     if (bn == 128) return launch_bn<128, 6, 8>(g, w, s);
     return launch_bn<192, 4, 8>(g, w, s);
 }
