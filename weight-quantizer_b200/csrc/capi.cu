@@ -105,7 +105,7 @@ int wq_kernel_info(int device, wq_kernel_info_t* out) {
     if (e != cudaSuccess) return cuda_fail(e);
     out->device_cc = prop.major * 10 + prop.minor;
     out->sm_count = prop.multiProcessorCount;
-    std::snprintf(out->device_name, sizeof(out->device_name), "%s", prop.name);
+    std::snprintf(out->device_name, sizeof(out->device_name), "%.95s", prop.name);
     return WQ_OK;
 }
 
