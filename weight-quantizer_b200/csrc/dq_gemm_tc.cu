@@ -5,12 +5,12 @@
 // fp32 accuracy from fp16 operands:
 //
 //   * A = (q - zero) for one 128-row weight tile. Every code minus an integral
-//     zero point is an integer of magnitude <= 255, exact in fp16. Four
-//     dequant warps build A from TMA-loaded packed codes (int4: LOP3 with the
-//     fp16 exponent 0x6400 gives 1024 + code, HSUB2 of 1024 + zero gives the
-//     exact difference) and write it straight into tensor memory with
-//     tcgen05.st (lane = weight row, two fp16 per column), two 64-wide K tiles
-//     per A stage; the MMA reads A from tensor memory.
+//     zero point is an integer of magnitude <= 255, exact in fp16. Dequant
+//     warps build A from TMA-loaded packed codes (int4: LOP3 with the fp16
+//     exponent 0x6400 gives 1024 + code, HSUB2 of 1024 + zero gives the exact
+//     difference) and write it straight into tensor memory with tcgen05.st
+//     (lane = weight row, two fp16 per column), two 64-wide K tiles per A
+//     stage; the MMA reads A from tensor memory.
 //   * B = x' * S_b split into fp16 hi + lo planes by a prep kernel (x' = x *
 //     channel, S_b a per-batch-row power of two putting max|x'_b * S_b| in
 //     [2^13, 2^14)), so hi + lo carries ~22 significant bits of x'. The prep
@@ -19,22 +19,23 @@
 //     one batch tile is a single contiguous bulk copy.
 //   * D[m, n] = sum_{k in group} A * (hi + lo) accumulates in fp32 in tensor
 //     memory: one accumulator per quantization group, double-buffered, so the
-//     per-row group scale can be applied outside the MMA. Four epilogue warps
+//     per-row group scale can be applied outside the MMA. The epilogue warps
 //     read each finished group accumulator with tcgen05.ld, add
 //     scale[m, g] * D into register accumulators, and at the end write
-//     y[n, m] = acc * 2^-S_b.
+//     y[n, m] = acc * 2^-S_b (into every output buffer, or once through an
+//     NVLink-switch address, for the row-sharded multi-GPU layer).
 //
-// Roles (one CTA = one 128 x BN output tile, 12 warps): warp 0 bulk-copies the
-// x' planes into an NS-deep shared-memory ring; warp 10 loads packed codes
+// Roles (one CTA = one 128 x BN output tile). Warpgroup 0: warp 0 bulk-copies
+// the x' planes into an NS-deep shared-memory ring; warp 2 loads packed codes
 // (several K tiles per 2D TMA box, 128 bytes per row, 128-byte swizzle) into a
 // separate ring that the dequant warps release as soon as they have read it;
 // warp 1 allocates tensor memory and one thread issues tcgen05.mma (M = 128,
 // N = BN, K = 16, A from tensor memory) and tcgen05.commit, learning which
-// tiles are ready from one shared word that warp 11 publishes after waiting
-// on their barriers; warps 2-5 dequantize; warps 6-9 run the epilogue. All hand-offs are mbarriers; every
-// wait is bounded and, on expiry, records bit 0 in the library's fault word
-// and stops waiting. Every TMA and bulk load targets this CTA's own shared
-// memory only.
+// tiles are ready from one shared word that warp 3 publishes after waiting on
+// their barriers. Then one or two dequant warpgroups (see Cfg) and one
+// epilogue warpgroup. All hand-offs are mbarriers; every wait is bounded and,
+// on expiry, records bit 0 in the library's fault word and stops waiting.
+// Every TMA and bulk load targets this CTA's own shared memory only.
 //
 // Output tiles are rasterized in bands of 16 batch tiles so the x' planes of a
 // band stay resident in L2 while the weights stream about twice.
