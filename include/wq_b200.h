@@ -226,7 +226,10 @@ WQ_API int wq_ipc_close_handle(void* ptr, int64_t offset);
  * stream. y_all, when not NULL, is an NVLink-switch address (NVLS) that
  * reaches the same position in every rank's buffer: the decode and
  * tensor-core kernels then issue one multimem.st per value instead of n_out
- * stores, and y_out is used only by the fallback. */
+ * stores, and y_out is used only by the fallback. bias, when not NULL, is an
+ * fp32 [M] vector added to every output row by the kernels' epilogues (the
+ * reference adds it after the GEMM in Python, linear.py:99-100: the same
+ * single fp32 add). */
 WQ_API int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
                                      const uint8_t* q, int64_t M, int64_t q_cols,
                                      const float* scales, int64_t scale_rows, int64_t groups,
@@ -234,6 +237,7 @@ WQ_API int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
                                      const float* channel_scale, int64_t channel_len,
                                      int group_size, int bits,
                                      float* const* y_out, int n_out, int64_t ldy, float* y_all,
+                                     const float* bias,
                                      void* workspace, size_t workspace_bytes,
                                      void* stream);
 

@@ -96,7 +96,7 @@ def test_multi_output_and_ipc_validation(wq) -> None:
 
     def multi(n_out: int, outs=None, bits: int = 4, group_size: int = 8):  # type: ignore[no-untyped-def]
         return lib.wq_dequant_gemm_f32_multi(None, 1, 8, None, 2, 4, None, 2, 1, None, 2, 1, None, -1,
-                                             group_size, bits, outs, n_out, 2, None, None, 0, None)
+                                             group_size, bits, outs, n_out, 2, None, None, None, 0, None)
 
     assert multi(1, bits=3) == 3            # reference validation first
     assert multi(0) == 22                   # WQ_E_OUTPUTS

@@ -13,6 +13,7 @@ The directory name is not a Python identifier; import it with
 ``importlib.import_module("weight-quantizer_b200")``.
 """
 
+from .convert import iter_targets, quantize_model, weight_out_in
 from .gemm import dequant_gemm, kernel_info
 from .linear import QuantizedLinear
 from .pack import pack_int4, unpack_int4
@@ -39,8 +40,11 @@ __all__ = [
     "dequant_gemm",
     "dequantize_weight",
     "element_scales",
+    "iter_targets",
     "kernel_info",
     "pack_int4",
+    "quantize_model",
     "quantize_weight",
     "unpack_int4",
+    "weight_out_in",
 ]

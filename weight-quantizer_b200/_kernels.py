@@ -67,7 +67,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
-         _int, _int, _vp, _int, _i64, _vp, _vp, _sz, _vp],
+         _int, _int, _vp, _int, _i64, _vp, _vp, _vp, _sz, _vp],
     ),
 }
 
@@ -176,13 +176,16 @@ def dequant_gemm(
     nthreads: int = 0,
     *,
     out: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """y[B, M] = x[B, K] @ W_hat^T on the current CUDA stream.
+    """y[B, M] = x[B, K] @ W_hat^T (+ bias) on the current CUDA stream.
 
     Same arguments as ptqkit's ``_kernels.dequant_gemm``. Inputs are cast to
     fp32/uint8 and made contiguous like the reference's ``forcecast | c_style``
     arrays (dequant_gemm.cpp:223-226). ``nthreads`` is accepted and ignored.
     ``out`` may be a preallocated fp32 [B, M] view with unit column stride.
+    ``bias`` (fp32 [M], no reference counterpart at this level: ptqkit adds it
+    in QuantizedLinear.forward) is added in the kernels' epilogue.
     """
     del nthreads
     if x.ndim != 2:
@@ -216,17 +219,32 @@ def dequant_gemm(
     lib = library()
     ws_bytes = int(lib.wq_dequant_gemm_workspace_bytes(B, M, K, int(group_size), int(bits)))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
-    status = lib.wq_dequant_gemm_f32(
-        _ptr(x), B, K,
-        _ptr(q), M, int(q.shape[1]),
-        _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
-        _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
-        _ptr(channel_scale), ch_len,
-        int(group_size), int(bits),
-        _ptr(y), ldy,
-        _ptr(ws), ws_bytes,
-        _stream(dev),
-    )
+    if bias is None:
+        status = lib.wq_dequant_gemm_f32(
+            _ptr(x), B, K,
+            _ptr(q), M, int(q.shape[1]),
+            _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
+            _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
+            _ptr(channel_scale), ch_len,
+            int(group_size), int(bits),
+            _ptr(y), ldy,
+            _ptr(ws), ws_bytes,
+            _stream(dev),
+        )
+    else:
+        b = _bias_arg(bias, M, dev)
+        arr = (ctypes.c_void_p * 1)(ctypes.c_void_p(y.data_ptr() if y.numel() else 0))
+        status = lib.wq_dequant_gemm_f32_multi(
+            _ptr(x), B, K,
+            _ptr(q), M, int(q.shape[1]),
+            _ptr(scales), int(scales.shape[0]), int(scales.shape[1]),
+            _ptr(zeros), int(zeros.shape[0]), int(zeros.shape[1]),
+            _ptr(channel_scale), ch_len,
+            int(group_size), int(bits),
+            ctypes.cast(arr, ctypes.c_void_p), 1, ldy, None, _ptr(b),
+            _ptr(ws), ws_bytes,
+            _stream(dev),
+        )
     _check(status)
     return y
 
@@ -364,13 +382,15 @@ def dequant_gemm_multi(
     outputs: list[int],
     ldy: int,
     y_all: int = 0,
+    bias: torch.Tensor | None = None,
 ) -> None:
     """dequant_gemm writing the same [B, M] result (row stride ``ldy``) into
     every device pointer of ``outputs`` (this GPU's buffers or peer buffers
     mapped with :func:`ipc_open`). The first output must be on the inputs'
     device; the tensor-core path stores into all of them from its epilogue.
     ``y_all`` (nonzero) is an NVLink-switch address that reaches every rank's
-    buffer at once; the tensor-core epilogue then stores through it alone."""
+    buffer at once; the tensor-core epilogue then stores through it alone.
+    ``bias`` (fp32 [M]) is added to every output row in the kernels' epilogue."""
     if x.ndim != 2:
         raise ValueError("x must have shape [B, K]")
     if q.ndim != 2 or scales.ndim != 2 or zeros.ndim != 2:
@@ -401,10 +421,22 @@ def dequant_gemm_multi(
         _ptr(channel_scale), ch_len,
         int(group_size), int(bits),
         ctypes.cast(arr, ctypes.c_void_p), len(outputs), int(ldy), ctypes.c_void_p(int(y_all)) if y_all else None,
+        _ptr(_bias_arg(bias, int(q.shape[0]), dev)),
         _ptr(ws), ws_bytes,
         _stream(dev),
     )
     _check(status)
+
+
+def _bias_arg(bias: torch.Tensor | None, M: int, dev: torch.device) -> torch.Tensor | None:
+    if bias is None:
+        return None
+    if bias.device != dev:
+        raise ValueError("bias must be on the inputs' device")
+    bias = bias.to(dtype=torch.float32).contiguous().reshape(-1)
+    if int(bias.numel()) != M:
+        raise ValueError("bias does not match out_features")
+    return bias
 
 
 def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:

@@ -141,8 +141,8 @@ namespace {
 int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, int64_t q_cols,
              const float* scales, int64_t scale_rows, int64_t groups, const float* zeros, int64_t zero_rows,
              int64_t zero_groups, const float* channel_scale, int64_t channel_len, int group_size, int bits,
-             float* const* y_out, int n_out, int64_t ldy, float* y_all, void* workspace, size_t workspace_bytes,
-             void* stream) {
+             float* const* y_out, int n_out, int64_t ldy, float* y_all, const float* bias, void* workspace,
+             size_t workspace_bytes, void* stream) {
     // dequant_gemm.cpp:241-276, same order
     if (bits != 4 && bits != 8) return WQ_E_BITS;
     if (group_size <= 0) return WQ_E_GROUP_SIZE;
@@ -165,7 +165,8 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (K == 0) {
         for (int i = 0; i < n_out; ++i) {
-            cudaError_t e = wq::launch_fill_zero(y_out[i], B, M, ldy, s);
+            cudaError_t e = bias != nullptr ? wq::launch_fill_bias(y_out[i], B, M, ldy, bias, s)
+                                            : wq::launch_fill_zero(y_out[i], B, M, ldy, s);
             if (e != cudaSuccess) return cuda_fail(e);
         }
         return WQ_OK;
@@ -181,6 +182,7 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
     p.y = y_out[0];
     p.n_extra = 0;
     p.y_all = nullptr;
+    p.bias = bias;
     for (int i = 0; i < 7; ++i) p.y_extra[i] = nullptr;
     p.B = B;
     p.M = M;
@@ -259,7 +261,7 @@ int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
                         void* stream) {
     float* const outs[1] = {y};
     return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
-                    channel_len, group_size, bits, y == nullptr ? nullptr : outs, 1, ldy, nullptr, workspace,
+                    channel_len, group_size, bits, y == nullptr ? nullptr : outs, 1, ldy, nullptr, nullptr, workspace,
                     workspace_bytes, stream);
 }
 
@@ -269,11 +271,11 @@ int wq_dequant_gemm_f32_multi(const float* x, int64_t B, int64_t K,
                               const float* zeros, int64_t zero_rows, int64_t zero_groups,
                               const float* channel_scale, int64_t channel_len,
                               int group_size, int bits,
-                              float* const* y_out, int n_out, int64_t ldy, float* y_all,
+                              float* const* y_out, int n_out, int64_t ldy, float* y_all, const float* bias,
                               void* workspace, size_t workspace_bytes,
                               void* stream) {
     return run_gemm(x, B, K, q, M, q_cols, scales, scale_rows, groups, zeros, zero_rows, zero_groups, channel_scale,
-                    channel_len, group_size, bits, y_out, n_out, ldy, y_all, workspace, workspace_bytes, stream);
+                    channel_len, group_size, bits, y_out, n_out, ldy, y_all, bias, workspace, workspace_bytes, stream);
 }
 
 size_t wq_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }

@@ -85,7 +85,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const GemmProblem p) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t m = m0 + tm * 4 + i;
-            if (m < p.M) p.y[b * p.ldy + m] = acc[i][j];
+            if (m < p.M) {
+                float v = acc[i][j];
+                if (p.bias != nullptr) v = __fadd_rn(v, p.bias[m]);   // linear.py:99-100, one fp32 add
+                p.y[b * p.ldy + m] = v;
+            }
         }
     }
 }
@@ -96,6 +100,16 @@ __global__ void fill_zero_kernel(float* y, int64_t B, int64_t M, int64_t ldy) {
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = i / M, m = i - b * M;
         y[b * ldy + m] = 0.0f;
+    }
+}
+
+// y = 0 + bias[m]: the reference's zero result plus its bias add.
+__global__ void fill_bias_kernel(float* y, int64_t B, int64_t M, int64_t ldy, const float* bias) {
+    const int64_t n = B * M;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / M, m = i - b * M;
+        y[b * ldy + m] = 0.0f + bias[m];
     }
 }
 
@@ -116,6 +130,15 @@ cudaError_t launch_fill_zero(float* y, int64_t B, int64_t M, int64_t ldy, cudaSt
     int64_t blocks = (n + 255) / 256;
     if (blocks > 4096) blocks = 4096;
     fill_zero_kernel<<<(unsigned)blocks, 256, 0, s>>>(y, B, M, ldy);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_bias(float* y, int64_t B, int64_t M, int64_t ldy, const float* bias, cudaStream_t s) {
+    const int64_t n = B * M;
+    if (n == 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    fill_bias_kernel<<<(unsigned)blocks, 256, 0, s>>>(y, B, M, ldy, bias);
     return cudaGetLastError();
 }
 

@@ -104,6 +104,7 @@ struct TcParams {
     float* y_extra[7];    // further outputs with y's layout (peer-mapped on other GPUs)
     int n_extra;
     float* y_all;         // NVLink-switch address reaching every rank's y, or nullptr
+    const float* bias;    // [M] or nullptr
     unsigned int* fault;
     int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
@@ -633,6 +634,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             if (g + 5 < p.ngroups) sc_n4 = __ldg(srow_p + g + 5);
         }
         if (m < p.M) {
+            // y = acc * 2^-S_b, then the layer's bias (linear.py:99-100) as one
+            // fp32 add after the product, like the reference (the _rn intrinsics
+            // keep the two roundings apart). Without a bias the add is of -0.0,
+            // which returns every value unchanged.
+            const float bm = p.bias != nullptr ? __ldg(p.bias + m) : -0.0f;
             // Every output buffer gets the tile; stores to peer-mapped buffers
             // travel over NVLink while other tiles still compute. No fence:
             // the kernel's completion makes its peer stores visible to work
@@ -642,7 +648,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
 #pragma unroll
                 for (int i = 0; i < BN; ++i) {
                     const int n = n0 + i;
-                    if (n < p.B) st_all_ranks(p.y_all + (int64_t)n * p.ldy + m, acc[i] * __ldg(p.inv_s + n));
+                    if (n < p.B)
+                        st_all_ranks(p.y_all + (int64_t)n * p.ldy + m, __fadd_rn(__fmul_rn(acc[i], __ldg(p.inv_s + n)), bm));
                 }
             } else {
                 for (int d = 0; d <= p.n_extra; ++d) {
@@ -650,7 +657,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
 #pragma unroll
                     for (int i = 0; i < BN; ++i) {
                         const int n = n0 + i;
-                        if (n < p.B) dst[(int64_t)n * p.ldy + m] = acc[i] * __ldg(p.inv_s + n);
+                        if (n < p.B) dst[(int64_t)n * p.ldy + m] = __fadd_rn(__fmul_rn(acc[i], __ldg(p.inv_s + n)), bm);
                     }
                 }
             }
@@ -794,6 +801,7 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.y = g.y;
     p.n_extra = g.n_extra;
     p.y_all = g.y_all;
+    p.bias = g.bias;
     for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;

@@ -117,6 +117,7 @@ struct GemvParams {
     float* y_extra[7];   // further outputs with y's layout (peer-mapped on other GPUs)
     int n_extra;
     float* y_all;        // NVLink-switch address reaching every rank's y, or nullptr
+    const float* bias;   // [M] or nullptr
     unsigned int* fault;
     int M, K, NCH;
     int64_t q_stride, ldy;
@@ -395,7 +396,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
                     for (int bb = 0; bb < NB; ++bb)
                         if (bb == b) e = eb[bb];
                     const int h = 25 + e, h1 = h / 2;
-                    const float out = (v * pow2i(h1)) * pow2i(h - h1);
+                    float out = (v * pow2i(h1)) * pow2i(h - h1);
+                    if (p.bias != nullptr) out = __fadd_rn(out, p.bias[row]);   // linear.py:99-100
                     const int64_t off = (int64_t)b * p.ldy + row;
                     if (p.y_all != nullptr) {
                         asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(p.y_all + off), "f"(out) : "memory");
@@ -559,6 +561,7 @@ cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t 
     p.y = g.y;
     p.n_extra = g.n_extra;
     p.y_all = g.y_all;
+    p.bias = g.bias;
     for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;

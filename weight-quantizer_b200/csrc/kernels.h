@@ -18,6 +18,7 @@ struct GemmProblem {
     float* y_extra[7];     // further outputs with y's layout (peer-mapped or local)
     int n_extra;           // entries of y_extra in use
     float* y_all;          // NVLink-switch address reaching every rank's y, or nullptr
+    const float* bias;     // [M] added to every output row, or nullptr
     int64_t B, M, K;
     int64_t q_stride;      // bytes per stored row: K (int8) or (K+1)/2 (int4)
     int64_t ldy;
@@ -43,8 +44,9 @@ cudaError_t launch_tc(const GemmProblem& p, void* workspace, cudaStream_t s);
 // --- generic tiled SIMT kernel: any shape, reference per-element formula ---
 cudaError_t launch_gemm_simt(const GemmProblem& p, cudaStream_t s);
 
-// --- zero-fill of y for K == 0 ---------------------------------------------
+// --- y for K == 0: zeros, or the bias in every row ---------------------------
 cudaError_t launch_fill_zero(float* y, int64_t B, int64_t M, int64_t ldy, cudaStream_t s);
+cudaError_t launch_fill_bias(float* y, int64_t B, int64_t M, int64_t ldy, const float* bias, cudaStream_t s);
 
 // --- RTN quantize + pack -----------------------------------------------------
 struct RtnProblem {

@@ -36,12 +36,16 @@ def dequant_gemm(
     impl: str = "reference",
     nthreads: int = 0,
     out: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Apply a quantized weight. ``x`` is [..., in]. Output is [..., out] (gemm.py:27-59).
 
     ``nthreads`` is accepted for signature compatibility and ignored. ``out``
     (kernel path) may be a preallocated fp32 [N, out] tensor for the flattened
-    batch; it is returned reshaped.
+    batch; it is returned reshaped. ``bias`` (an extension: ptqkit adds the
+    bias in ``QuantizedLinear.forward``, linear.py:99-100) is added to every
+    output row, in the kernels' epilogue on the kernel path; the result is the
+    same single fp32 add.
     """
     if impl not in ("reference", "kernel"):
         raise ValueError("impl must be 'reference' or 'kernel'")
@@ -51,6 +55,8 @@ def dequant_gemm(
     flat = x.detach().reshape(-1, qw.in_features).to(dtype=torch.float32)
     if impl == "reference":
         y = flat @ dequantize_weight(qw).transpose(0, 1)
+        if bias is not None:
+            y = y + bias
     else:
         if flat.device.type != "cuda":
             raise RuntimeError("the dequant kernel runs on CUDA")
@@ -64,5 +70,6 @@ def dequant_gemm(
             int(qw.bits),
             int(nthreads),
             out=out,
+            bias=None if bias is None else bias.detach(),
         )
     return y.reshape(*lead, qw.out_features)

@@ -97,6 +97,9 @@ class QuantizedLinear(nn.Module):
         flat = x.reshape(-1, self.in_features)
         if self._cached is not None:
             y = nn.functional.linear(flat, self._cached, self.bias)
+        elif self.impl == "kernel":
+            # the bias add (linear.py:99-100) happens in the kernel's epilogue
+            y = dequant_gemm(flat, self.quantized_weight(), impl="kernel", bias=self.bias)
         else:
             y = dequant_gemm(flat, self.quantized_weight(), impl=self.impl)
             if self.bias is not None:
