@@ -12,7 +12,8 @@ src/ptqkit/measure.py:167, dequantization not counted), whole job, t = max over
 ranks of the CUDA-event time of K steps. Also reported: the same layer at the
 decode batches 1, 32 and 256 (weight-stream GB/s and GFLOP/s), the end-to-end
 number through the public API with host buffers, the dominant kernel's
-roofline, and the reference CPU kernel timed on this host.
+roofline, the layer saved in ptqkit's compressed format and loaded back
+(``loader``), and the reference CPU kernel timed on this host.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -183,6 +184,52 @@ def cpu_baseline_sample(q: Any, scales: Any, zeros: Any, x: Any, seconds: float)
             "cores": threads, "kind": "reference" if kern is not None else "port",
             "sample": f"batch {x.shape[0]} x full {M_ROWS}x{K_COLS} layer, median of {len(times)} calls "
                       f"({'ptqkit _kernels.dequant_gemm built in oracle/_ref' if kern else 'C oracle'})"}
+
+
+def loader_line(wq: Any, qw: Any, dev: Any, stream: Any, peaks: dict[str, Any]) -> dict[str, Any]:
+    """The layer (with an fp32 bias) saved in ptqkit's compressed format and
+    loaded back through load_compressed_layers, three times, wall clock with
+    the device synchronized (the file is in the page cache); plus the widening
+    kernel alone on 64 Mi fp16 values, timed with CUDA events."""
+    import torch
+
+    bias = torch.randn(qw.out_features, generator=torch.Generator().manual_seed(5)).to(dev)
+    layer = wq.QuantizedLinear(qw, bias, impl="kernel")
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "layer.pt")
+        t0 = time.perf_counter()
+        size = wq.save_compressed(layer, path)
+        t_save = time.perf_counter() - t0
+        times = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            loaded = wq.load_compressed_layers(path, device=dev)[""]
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+        same = bool(torch.equal(loaded.codes, layer.codes)
+                    and torch.equal(loaded.scales, layer.scales.half().float()))
+    payload = int(layer.codes.nbytes + 2 * (layer.scales.numel() + layer.zeros.numel()) + 4 * bias.numel())
+    t_load = sorted(times)[1]
+    n = 64 * 1024 * 1024
+    src = torch.randn(n, device=dev).half()
+    dst = torch.empty(n, dtype=torch.float32, device=dev)
+    ev = []
+    for i in range(8):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        wq._kernels.widen_f16_f32(src, dst)
+        e1.record(stream)
+        if i >= 3:
+            ev.append((e0, e1))
+    torch.cuda.synchronize()
+    t_w = sum(a.elapsed_time(b) for a, b in ev) / len(ev) / 1e3
+    widen_gbs = 6.0 * n / t_w / 1e9
+    return {"layer": "28672x8192 int4 g128 + fp32 bias", "file_bytes": size, "payload_bytes": payload,
+            "save_ms": round(t_save * 1e3, 1), "load_ms": round(t_load * 1e3, 2),
+            "load_gbs": round(payload / t_load / 1e9, 2), "loaded_equals_rounded": same,
+            "widen": {"values": n, "us": round(t_w * 1e6, 1), "gbs": round(widen_gbs, 1),
+                      "frac_hbm": round(widen_gbs / peaks["hbm_gbs"], 4)}}
 
 
 def ours(args: argparse.Namespace) -> None:
@@ -384,6 +431,11 @@ def ours(args: argparse.Namespace) -> None:
                        + (" storing y into every rank over NVLink" if world > 1 else "")
                        + "), its 1/N of y rows -> pinned host"}
 
+    # ---- compressed-format loader: this layer written and read back ---------
+    loader = None
+    if rank == 0 and world == 1 and not args.no_loader:
+        loader = loader_line(wq, full_qw, dev, stream, peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = min(args.cpu_sample_rows, B)
@@ -408,6 +460,7 @@ def ours(args: argparse.Namespace) -> None:
             "roofline": roofline,
             "sweep": sweep,
             "e2e": e2e,
+            "loader": loader,
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * launches_per_step,
         }
@@ -428,6 +481,7 @@ def main() -> None:
     ap.add_argument("--sweep", type=lambda s: [int(v) for v in s.split(",") if v], default=[1, 32, 256])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-loader", action="store_true")
     ap.add_argument("--cpu-sample-rows", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

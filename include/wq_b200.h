@@ -194,6 +194,19 @@ WQ_API int wq_gather_permute_f32(const float* src, int64_t P, int64_t B, int64_t
                           float* dst, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Compressed format (version 1, src/ptqkit/convert.py:296-336): codes are   */
+/* stored as they are; scales, zeros and the channel scale in fp16. ptqkit   */
+/* has no loader; these two passes serve this library's loader (one upload  */
+/* of every layer's fp16 payload, widened in one launch into the fp32        */
+/* arrays the dequant-GEMM reads) and its writer.                            */
+/* ------------------------------------------------------------------------ */
+/* dst[i] = (float)src[i] for n fp16 values (exact). */
+WQ_API int wq_widen_f16_f32(const uint16_t* src, float* dst, int64_t n, void* stream);
+/* dst[i] = fp16(src[i]), round to nearest even, overflow to infinity: the
+ * `.to(dtype=torch.float16)` of compressed_state (convert.py:318-323). */
+WQ_API int wq_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */
 /* whose kernel runs on one CPU and splits rows across OpenMP threads        */
 /* (dequant_gemm.cpp:196-205). Each rank computes its rows of y; the         */

@@ -13,6 +13,16 @@ The directory name is not a Python identifier; import it with
 ``importlib.import_module("weight-quantizer_b200")``.
 """
 
+from .compressed import (
+    compressed_state,
+    load_compressed,
+    load_compressed_layers,
+    matrix_nbytes,
+    payload_nbytes,
+    read_compressed,
+    save_compressed,
+    state_dict_nbytes,
+)
 from .convert import iter_targets, quantize_model, weight_out_in
 from .gemm import dequant_gemm, kernel_info
 from .linear import QuantizedLinear
@@ -37,14 +47,22 @@ __all__ = [
     "QuantizedWeight",
     "absolute_error_bound",
     "assemble_quantized",
+    "compressed_state",
     "dequant_gemm",
     "dequantize_weight",
     "element_scales",
     "iter_targets",
     "kernel_info",
+    "load_compressed",
+    "load_compressed_layers",
+    "matrix_nbytes",
     "pack_int4",
+    "payload_nbytes",
     "quantize_model",
     "quantize_weight",
+    "read_compressed",
+    "save_compressed",
+    "state_dict_nbytes",
     "unpack_int4",
     "weight_out_in",
 ]

@@ -60,6 +60,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
          _int, _int, _vp, _i64, _vp],
     ),
+    "wq_widen_f16_f32": (_int, [_vp, _vp, _i64, _vp]),
+    "wq_narrow_f32_f16": (_int, [_vp, _vp, _i64, _vp]),
     "wq_ipc_handle_bytes": (_sz, []),
     "wq_ipc_get_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int64)]),
     "wq_ipc_open_handle": (_int, [_vp, _i64, ctypes.POINTER(ctypes.c_void_p)]),
@@ -459,3 +461,31 @@ def ipc_open(handle: bytes, offset: int) -> int:
 
 def ipc_close(ptr: int, offset: int) -> None:
     _check(library().wq_ipc_close_handle(ctypes.c_void_p(int(ptr)), int(offset)))
+
+
+def widen_f16_f32(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 -> fp32 (exact) on the device; ``out`` (fp32, same element count) is
+    written in place when given. Used by the compressed-format loader."""
+    dev = _cuda_device([src] if out is None else [src, out])
+    if src.dtype != torch.float16:
+        raise ValueError("widen_f16_f32 expects a float16 tensor")
+    s = src.contiguous()
+    dst = out if out is not None else torch.empty(s.shape, dtype=torch.float32, device=dev)
+    if dst.dtype != torch.float32 or not dst.is_contiguous() or dst.numel() != s.numel():
+        raise ValueError("out must be a contiguous float32 tensor with the input's element count")
+    _check(library().wq_widen_f16_f32(_ptr(s), _ptr(dst), int(s.numel()), _stream(dev)))
+    return dst
+
+
+def narrow_f32_f16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 -> fp16 (round to nearest even) on the device, as compressed_state
+    stores scales, zeros and channel scales (convert.py:318-323)."""
+    dev = _cuda_device([src] if out is None else [src, out])
+    if src.dtype != torch.float32:
+        raise ValueError("narrow_f32_f16 expects a float32 tensor")
+    s = src.contiguous()
+    dst = out if out is not None else torch.empty(s.shape, dtype=torch.float16, device=dev)
+    if dst.dtype != torch.float16 or not dst.is_contiguous() or dst.numel() != s.numel():
+        raise ValueError("out must be a contiguous float16 tensor with the input's element count")
+    _check(library().wq_narrow_f32_f16(_ptr(s), _ptr(dst), int(s.numel()), _stream(dev)))
+    return dst

@@ -399,4 +399,18 @@ int wq_gather_permute_f32(const float* src, int64_t P, int64_t B, int64_t Mp, fl
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 
+int wq_widen_f16_f32(const uint16_t* src, float* dst, int64_t n, void* stream) {
+    if (n < 0) return WQ_E_NEG_DIM;
+    if (n > 0 && (src == nullptr || dst == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_widen_f16_f32(src, dst, n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, void* stream) {
+    if (n < 0) return WQ_E_NEG_DIM;
+    if (n > 0 && (src == nullptr || dst == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_narrow_f32_f16(src, dst, n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
 }  // extern "C"

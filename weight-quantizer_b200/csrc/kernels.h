@@ -74,6 +74,10 @@ cudaError_t launch_dequantize(const uint8_t* q, int64_t M, int64_t K, int64_t q_
 cudaError_t launch_gather_permute(const float* src, int64_t P, int64_t B, int64_t Mp, float* dst,
                                   cudaStream_t s);
 
+// --- compressed format: fp16 payload <-> fp32 kernel arrays ----------------
+cudaError_t launch_widen_f16_f32(const uint16_t* src, float* dst, int64_t n, cudaStream_t s);
+cudaError_t launch_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, cudaStream_t s);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
