@@ -101,7 +101,12 @@ def test_shapes_sweep_vs_oracle(wq, orc, cuda, bits: int, batch: int) -> None:
     g = torch.Generator().manual_seed(100 + bits * 10 + batch)
     shapes = [(96, 256, 128, True, False), (130, 1024, 64, False, True), (33, 4095, 64, True, False),
               (64, 768, None, False, False), (50, 300, 0, True, False), (17, 13, 3, False, False),
-              (40, 2048, 32, True, True), (257, 512, 512, False, False)]
+              (40, 2048, 32, True, True), (257, 512, 512, False, False),
+              # int4 batches 1-2 on the integer tensor-core decode kernel: one
+              # table for all rows, full 8192-wide K slices at F = 128 and 64,
+              # per-channel tables with a partial last row block
+              (64, 512, 0, True, False), (48, 8192, 128, True, True), (32, 8192, 64, False, False),
+              (20, 1024, None, True, False)]
     for (M, K, group, sym, pre) in shapes:
         qw = _rand_layer(wq, g, M, K, bits, sym, group, pre)
         x = torch.randn(batch, K, generator=g)

@@ -538,6 +538,7 @@ size_t gemv_workspace_bytes(int64_t, int64_t, int) { return 0; }
 
 bool gemv_supported(const GemmProblem& p) {
     if (p.B < 1 || p.B > kGemvMaxBatch || p.K < 1 || p.M < 1) return false;
+    if (gemv_imma_supported(p)) return true;
     if (p.q_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(p.q) & 15) != 0) return false;
     const int CH = p.bits == 4 ? 32 : 16;
     if (p.groups > 1 && (p.group_size % CH) != 0) return false;
@@ -552,6 +553,7 @@ bool gemv_supported(const GemmProblem& p) {
 }
 
 cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t s) {
+    if (gemv_imma_supported(g)) return launch_gemv_imma(g, s);
     GemvParams p;
     p.x = g.x;
     p.q = g.q;

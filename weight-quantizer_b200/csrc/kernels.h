@@ -33,6 +33,11 @@ size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
 // batch, shared-memory fit).
 bool gemv_supported(const GemmProblem& p);
 cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
+// int4 codes at batches 1-2 on the integer tensor-core path (mma.sync u4 x s4),
+// when groups are multiples of 64 (or one group), K <= 8192 and the tables
+// can be bulk-copied; launch_gemv routes these problems to it.
+bool gemv_imma_supported(const GemmProblem& p);
+cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
 
 // --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
 // Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
