@@ -536,9 +536,27 @@ cudaError_t dispatch(const GemvParams& p, int NB, int ncpl, bool lean, cudaStrea
 
 size_t gemv_workspace_bytes(int64_t, int64_t, int) { return 0; }
 
+// Batch rows [r0, r0 + nb) of a problem: the same layer, x and every output
+// advanced by r0 rows.
+static GemmProblem batch_rows(const GemmProblem& g, int64_t r0, int64_t nb) {
+    GemmProblem h = g;
+    h.B = nb;
+    h.x = g.x + r0 * g.K;
+    h.y = g.y + r0 * g.ldy;
+    for (int d = 0; d < g.n_extra; ++d) h.y_extra[d] = g.y_extra[d] + r0 * g.ldy;
+    if (g.y_all != nullptr) h.y_all = g.y_all + r0 * g.ldy;
+    return h;
+}
+
+// Batches 3-4 that the tensor-core decode kernel takes as two launches.
+static bool imma_split(const GemmProblem& p) {
+    return (p.B == 3 || p.B == 4) && gemv_imma_supported(batch_rows(p, 0, 2)) &&
+           gemv_imma_supported(batch_rows(p, 2, p.B - 2));
+}
+
 bool gemv_supported(const GemmProblem& p) {
     if (p.B < 1 || p.B > kGemvMaxBatch || p.K < 1 || p.M < 1) return false;
-    if (gemv_imma_supported(p)) return true;
+    if (gemv_imma_supported(p) || imma_split(p)) return true;
     if (p.q_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(p.q) & 15) != 0) return false;
     const int CH = p.bits == 4 ? 32 : 16;
     if (p.groups > 1 && (p.group_size % CH) != 0) return false;
@@ -554,6 +572,15 @@ bool gemv_supported(const GemmProblem& p) {
 
 cudaError_t launch_gemv(const GemmProblem& g, void* /*workspace*/, cudaStream_t s) {
     if (gemv_imma_supported(g)) return launch_gemv_imma(g, s);
+    // Batches 3-4 of an int4 layer the tensor-core decode kernel takes: two
+    // passes over the weights (rows 0-1, then the rest) stream less time than
+    // one pass of the SIMT kernel, whose activations for 3-4 rows crowd its
+    // registers.
+    if (imma_split(g)) {
+        cudaError_t e = launch_gemv_imma(batch_rows(g, 0, 2), s);
+        if (e != cudaSuccess) return e;
+        return launch_gemv_imma(batch_rows(g, 2, g.B - 2), s);
+    }
     GemvParams p;
     p.x = g.x;
     p.q = g.q;

@@ -45,6 +45,8 @@
 // refills the stage. Every mbarrier wait is bounded; on expiry the kernel
 // sets bit 0 of the library's fault word and runs to completion without
 // waiting again.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -53,7 +55,7 @@ namespace {
 
 constexpr int kImmaWarps = 8;                  // warps that multiply
 constexpr int kImmaThreads = (kImmaWarps + 1) * 32;   // + one producer warp
-constexpr int kImmaRows = 16;                  // rows per stage: the MMA's M
+constexpr int kImmaRows = 16;                  // rows an MMA (and a stage) holds; a row block uses rb <= 16
 constexpr int kSliceCodes = 1024;              // most codes of a row one warp covers
 constexpr int kLimbs = 3;                      // base-256 digits of a 23-bit signed integer
 constexpr int kDigRow = kSliceCodes / 8 * 2 + 4;  // words per limb row: (even, odd) per octet, +16 B skew
@@ -88,6 +90,7 @@ struct ImmaParams {
     int ts;             // floats per table row inside a stage (0: shared table)
     int rs;             // bytes per code row inside a stage
     int ns;             // stages
+    int rb;             // rows per row block (<= 16; the MMA's other rows are ignored)
     int defer_last;     // the digit table borrows the last stage, which is filled after staging
     uint32_t stage_bytes;
     uint32_t shared_tab_bytes;
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const bool producer = warp == kImmaWarps;
-    const int n_blocks = (p.M + kImmaRows - 1) / kImmaRows;
+    const int n_blocks = (p.M + p.rb - 1) / p.rb;
     const uint32_t full0 = smem_addr(full);
     const uint32_t cons0 = smem_addr(consumed);
     const uint32_t tab_bytes = p.tables == kTabShared ? 0u : (uint32_t)(kImmaRows * p.ts * 4);
@@ -153,8 +156,8 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
     // the parity of the number of fills (producer lane 0)
     uint32_t filled = 0, fill_par = 0;
     auto issue = [&](int blk, int s) {
-        const int row0 = blk * kImmaRows;
-        const int rows = (p.M - row0) < kImmaRows ? (p.M - row0) : kImmaRows;
+        const int row0 = blk * p.rb;
+        const int rows = (p.M - row0) < p.rb ? (p.M - row0) : p.rb;
         const uint32_t dst = smem_addr(stages + (size_t)s * p.stage_bytes);
         const uint32_t bar = full0 + 8u * (uint32_t)s;
         uint32_t tb = 0;
@@ -327,9 +330,11 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
                     bw[i][v] = q4.x; bw[i][v + 1] = q4.y; bw[i][v + 2] = q4.z; bw[i][v + 3] = q4.w;
                 }
             }
-            const float2 pf = fbt_w[lane_b * FBW + i];
-            pw[i] = pf.x;
-            zq[i] = zero_lane ? pf.y : 0.0f;
+            if constexpr (!FAST) {
+                const float2 pf = fbt_w[lane_b * FBW + i];
+                pw[i] = pf.x;
+                zq[i] = zero_lane ? pf.y : 0.0f;
+            }
         }
     }
     named_barrier(1, kImmaThreads);   // mbarrier init, shared table and every lane's reads of the digit table
@@ -355,9 +360,9 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
             faulted = __shfl_sync(0xffffffffu, faulted ? 1 : 0, 0) != 0;
             __syncwarp();
             const float* rb = red + (size_t)s * kImmaWarps * kImmaRows * NB;
-            if (lane < kImmaRows * NB) {
-                const int r = lane & (kImmaRows - 1), b = lane >> 4;
-                const int row = blk * kImmaRows + r;
+            const int r = lane & (kImmaRows - 1), b = lane >> 4;
+            if (lane < kImmaRows * NB && r < p.rb) {
+                const int row = blk * p.rb + r;
                 float v = 0.0f;
 #pragma unroll
                 for (int w = 0; w < kImmaWarps; ++w) v += rb[(w * kImmaRows + r) * NB + b];
@@ -397,6 +402,7 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
     }
 
     // ---- multiply warps: stream rows ----------------------------------------
+    const float2* fbt_lane = fbt_w + lane_b * FBW;
     bool faulted = false;
     int s = 0;
     uint32_t phase = 0;
@@ -451,10 +457,14 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
                     mma_u8s8(c1, lo_nibbles(ag[mm + 1]), lo_nibbles(ah[mm + 1]), hi_nibbles(ag[mm + 1]),
                              hi_nibbles(ah[mm + 1]), bw[i][2 * mm + 2], bw[i][2 * mm + 3]);
                 }
-                const float v0 = fmaf((float)((c0[0] + c1[0]) + mB * (c0[1] + c1[1])), wC, -zg[i] * zq[i]);
-                const float v1 = fmaf((float)((c0[2] + c1[2]) + mB * (c0[3] + c1[3])), wC, -zh[i] * zq[i]);
-                acc0 = fmaf(sg[i] * pw[i], v0, acc0);
-                acc1 = fmaf(sh[i] * pw[i], v1, acc1);
+                // the fold block's factors come from shared memory (a broadcast
+                // load) rather than registers, which this variant has none to spare
+                const float2 pf = fbt_lane[i];
+                const float zqi = zero_lane ? pf.y : 0.0f;
+                const float v0 = fmaf((float)((c0[0] + c1[0]) + mB * (c0[1] + c1[1])), wC, -zg[i] * zqi);
+                const float v1 = fmaf((float)((c0[2] + c1[2]) + mB * (c0[3] + c1[3])), wC, -zh[i] * zqi);
+                acc0 = fmaf(sg[i] * pf.x, v0, acc0);
+                acc1 = fmaf(sh[i] * pf.x, v1, acc1);
             }
         } else {
             const float* tsc_g = tsc + g * p.ts;
@@ -513,7 +523,7 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
 constexpr size_t kImmaSmemMax = 227 * 1024;
 
 struct ImmaPlan {
-    int F, FBW, fast, tables, ts, rs, ns, nfb, defer_last;
+    int F, FBW, fast, tables, ts, rs, ns, rb, nfb, defer_last;
     uint32_t stage_bytes, shared_tab_bytes, dig_off, fbt_off;
     size_t smem;
 };
@@ -595,18 +605,51 @@ bool imma_plan(const GemmProblem& g, ImmaPlan& pl) {
     return imma_layout<2, 16>(pl);
 }
 
+// Rows per row block: the value in [8, 16] whose last wave is fullest, i.e.
+// that minimizes (row blocks per CTA, rounded up) x rows per block; ties go
+// to more rows. Per-channel tables are copied whole, so there the block must
+// keep a multiple of 4 rows.
+int imma_rows_per_block(int64_t M, int grid_max, int tables) {
+    int best = kImmaRows;
+    int64_t best_cost = -1;
+    for (int rb = kImmaRows; rb >= 8; --rb) {
+        if (tables == kTabColumn && rb % 4 != 0) continue;
+        const int64_t nb = (M + rb - 1) / rb;
+        const int64_t cost = (nb + grid_max - 1) / grid_max * rb;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = rb;
+        }
+    }
+    return best;
+}
+
 template <int NB, int F, int FBW, bool FAST>
-cudaError_t launch_imma_t(const ImmaParams& p, size_t smem, cudaStream_t s) {
+cudaError_t launch_imma_t(ImmaParams p, size_t smem, cudaStream_t s) {
     auto kern = gemv_imma_kernel<NB, F, FBW, FAST>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // The shared-memory opt-in and the occupancy for it are looked up once per
+    // device and shared-memory size (the last pair is kept).
+    constexpr int kDevs = 32;
+    static std::atomic<uint64_t> cache[kDevs];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kImmaThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    const int n_blocks = (p.M + kImmaRows - 1) / kImmaRows;
-    int grid = sm_count() * occ;
-    if (grid > n_blocks) grid = n_blocks;
+    const uint64_t c = (dev >= 0 && dev < kDevs) ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (c != 0 && (c >> 32) == (uint64_t)smem) {
+        occ = (int)(c & 0xFFFFFFFFu);
+    } else {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kImmaThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (occ < 1) return cudaErrorInvalidConfiguration;
+        if (dev >= 0 && dev < kDevs) cache[dev].store(((uint64_t)smem << 32) | (uint32_t)occ, std::memory_order_relaxed);
+    }
+    const int grid_max = sm_count() * occ;
+    p.rb = imma_rows_per_block(p.M, grid_max, p.tables);
+    const int n_blocks = (p.M + p.rb - 1) / p.rb;
+    int grid = grid_max < n_blocks ? grid_max : n_blocks;
     if (grid < 1) grid = 1;
     kern<<<grid, kImmaThreads, smem, s>>>(p);
     return cudaGetLastError();
@@ -656,6 +699,7 @@ cudaError_t launch_gemv_imma(const GemmProblem& g, cudaStream_t s) {
     p.ts = pl.ts;
     p.rs = pl.rs;
     p.ns = pl.ns;
+    p.rb = kImmaRows;
     p.defer_last = pl.defer_last;
     p.stage_bytes = pl.stage_bytes;
     p.shared_tab_bytes = pl.shared_tab_bytes;
