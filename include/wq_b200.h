@@ -207,6 +207,28 @@ WQ_API int wq_widen_f16_f32(const uint16_t* src, float* dst, int64_t n, void* st
 WQ_API int wq_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* AWQ alpha search (src/ptqkit/awq.py:39-81) and its calibration statistic  */
+/* (src/ptqkit/convert.py:35-63). The search quantizes W diag(s) with        */
+/* wq_rtn_quantize_f32 and scores it with wq_dequant_gemm_f32; these are the */
+/* reductions around them. All are deterministic (fixed summation order).    */
+/* ------------------------------------------------------------------------ */
+/* acc[k] += sum_i |x[i, k]| over the n rows of x (fp32, row stride ldx      */
+/* >= K), summed in fp64 in row order: ActivationStats.update's               */
+/* x64.abs().sum(dim=0) (convert.py:47-48); divided by n it is awq.py:61's    */
+/* activations.abs().mean(dim=0). acc is fp64 [K] on the device.             */
+WQ_API int wq_channel_abs_sum_f64(const float* x, int64_t n, int64_t K, int64_t ldx, double* acc, void* stream);
+/* pre[k] = mag[k]^alpha / max(mean_j mag[j]^alpha, 1e-8) (awq.py:70-74, mag */
+/* already clamped to >= 1e-8 by the caller as awq.py:61-65 does); alpha = 0 */
+/* writes 1 (awq.py:68-69). The mean is taken in fp64 and rounded to fp32.    */
+WQ_API int wq_awq_pre_scale_f32(const float* mag, int64_t K, float alpha, float* pre, void* stream);
+/* out[0] = sum_i (a[i] - b[i])^2 over n fp32 values, in fp64: the numerator */
+/* of awq.py:76-77's err.square().mean(). workspace: device memory of        */
+/* wq_sq_err_workspace_bytes() bytes.                                         */
+WQ_API size_t wq_sq_err_workspace_bytes(void);
+WQ_API int wq_sq_err_sum_f64(const float* a, const float* b, int64_t n, double* out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */
 /* whose kernel runs on one CPU and splits rows across OpenMP threads        */
 /* (dequant_gemm.cpp:196-205). Each rank computes its rows of y; the         */

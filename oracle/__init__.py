@@ -184,3 +184,64 @@ def reference_kernels() -> ModuleType | None:
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module
+
+
+def dequantize(codes: np.ndarray, scales: np.ndarray, zeros: np.ndarray, channel: np.ndarray | None,
+               group_size: int) -> np.ndarray:
+    """W_hat in fp32 with quant.py:292-308's operation order: (codes - zero) * scale [* channel]."""
+    codes = np.asarray(codes, dtype=np.float32)
+    idx = np.arange(codes.shape[1]) // group_size
+    rows = scales.shape[0]
+    sc = scales[0, idx][None, :] if rows == 1 else scales[:, idx]
+    zr = zeros[0, idx][None, :] if rows == 1 else zeros[:, idx]
+    hat = ((codes - zr).astype(np.float32) * sc).astype(np.float32)
+    if channel is not None:
+        hat = (hat * channel[None, :]).astype(np.float32)
+    return hat
+
+
+def awq_search(
+    w: np.ndarray,
+    x: np.ndarray,
+    bits: int,
+    symmetric: bool,
+    group_size: int | None,
+    alphas: tuple[float, ...],
+    mean_abs: np.ndarray | None = None,
+) -> dict[str, object]:
+    """The alpha search of src/ptqkit/awq.py:39-81 restated in numpy plus this
+    package's C RTN: channel magnitudes and scores in fp64, pre-scales rounded
+    to fp32 as the reference does (m^alpha, then the division by the clamped
+    mean). Returns the winning alpha, every alpha's score and pre-scale, and the
+    winner's RTN outputs."""
+    w = _c(w, np.float32)
+    x = np.asarray(x, dtype=np.float32)
+    if mean_abs is None:
+        mag = np.abs(x.astype(np.float64)).mean(axis=0).astype(np.float32)
+    else:
+        mag = np.asarray(mean_abs, dtype=np.float32).reshape(-1)
+    mag = np.maximum(mag, np.float32(1e-8))
+    n = x.shape[0]
+    search = x if n <= 2048 else x[:: max(n // 2048, 1)][:2048]
+    s64 = search.astype(np.float64)
+    target = s64 @ w.astype(np.float64).T
+    best_alpha, best_mse, best = float(alphas[0]), float("inf"), None
+    mses, pres = [], []
+    for a in alphas:
+        a = float(a)
+        if a == 0.0:
+            pre = np.ones(w.shape[1], dtype=np.float32)
+        else:
+            p = (mag.astype(np.float64) ** a).astype(np.float32)
+            mean = np.float32(p.astype(np.float64).mean())
+            mean = max(mean, np.float32(1e-8))
+            pre = (p / mean).astype(np.float32)
+        r = rtn_quantize(w, bits, symmetric, group_size, pre)
+        hat = dequantize(r["codes"], r["scales"], r["zeros"], r["channel_scale"], int(r["group_size"]))
+        err = s64 @ hat.astype(np.float64).T - target
+        mse = float((err * err).mean()) if err.size else float("nan")
+        mses.append(mse)
+        pres.append(pre)
+        if mse < best_mse:
+            best_alpha, best_mse, best = a, mse, r
+    return {"alpha": best_alpha, "mse": mses, "pre_scale": pres, "rtn": best, "mag": mag}

@@ -66,6 +66,10 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_ipc_get_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int64)]),
     "wq_ipc_open_handle": (_int, [_vp, _i64, ctypes.POINTER(ctypes.c_void_p)]),
     "wq_ipc_close_handle": (_int, [_vp, _i64]),
+    "wq_channel_abs_sum_f64": (_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "wq_awq_pre_scale_f32": (_int, [_vp, _i64, ctypes.c_float, _vp, _vp]),
+    "wq_sq_err_workspace_bytes": (_sz, []),
+    "wq_sq_err_sum_f64": (_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
@@ -489,3 +493,52 @@ def narrow_f32_f16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.
         raise ValueError("out must be a contiguous float16 tensor with the input's element count")
     _check(library().wq_narrow_f32_f16(_ptr(s), _ptr(dst), int(s.numel()), _stream(dev)))
     return dst
+
+
+# ---- AWQ search reductions (src/ptqkit/awq.py:39-81, convert.py:35-63) -------
+
+
+def channel_abs_sum(x: torch.Tensor, acc: torch.Tensor | None = None) -> torch.Tensor:
+    """acc[k] += sum_i |x[i, k]| in fp64 (rows in order); returns acc (fp64 [K]).
+
+    ActivationStats.update's ``x64.abs().sum(dim=0)`` (convert.py:47-48); a new
+    zeroed accumulator is made when ``acc`` is None.
+    """
+    if x.ndim != 2:
+        raise ValueError("activations must have shape [n, in]")
+    dev = _cuda_device([x])
+    x = x.to(dtype=torch.float32)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n, k = int(x.shape[0]), int(x.shape[1])
+    if acc is None:
+        acc = torch.zeros(k, dtype=torch.float64, device=dev)
+    elif acc.dtype != torch.float64 or acc.device != dev or int(acc.numel()) != k or not acc.is_contiguous():
+        raise ValueError("acc must be a contiguous fp64 [in] tensor on the activations' device")
+    ld = int(x.stride(0)) if n > 1 else k
+    _check(library().wq_channel_abs_sum_f64(_ptr(x), n, k, ld, _ptr(acc), _stream(dev)))
+    return acc
+
+
+def awq_pre_scale(mag: torch.Tensor, alpha: float) -> torch.Tensor:
+    """s = mag^alpha / max(mean(mag^alpha), 1e-8) in fp32 (awq.py:68-74); 1 for alpha = 0."""
+    dev = _cuda_device([mag])
+    m = mag.to(dtype=torch.float32).contiguous().reshape(-1)
+    pre = torch.empty_like(m)
+    _check(library().wq_awq_pre_scale_f32(_ptr(m), int(m.numel()), float(alpha), _ptr(pre), _stream(dev)))
+    return pre
+
+
+def sq_err_sum(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """sum (a - b)^2 over all elements, in fp64, as a device scalar (awq.py:76-77)."""
+    if a.shape != b.shape:
+        raise ValueError("operands must have the same shape")
+    dev = _cuda_device([a, b])
+    a = a.to(dtype=torch.float32).contiguous()
+    b = b.to(dtype=torch.float32).contiguous()
+    lib = library()
+    ws_bytes = int(lib.wq_sq_err_workspace_bytes())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    out = torch.empty((), dtype=torch.float64, device=dev)
+    _check(lib.wq_sq_err_sum_f64(_ptr(a), _ptr(b), int(a.numel()), _ptr(out), _ptr(ws), ws_bytes, _stream(dev)))
+    return out

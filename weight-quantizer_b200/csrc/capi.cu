@@ -413,4 +413,31 @@ int wq_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, void* stream) 
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 
+int wq_channel_abs_sum_f64(const float* x, int64_t n, int64_t K, int64_t ldx, double* acc, void* stream) {
+    if (n < 0 || K < 0) return WQ_E_NEG_DIM;
+    if (ldx < K) return WQ_E_LD;
+    if (K > 0 && (acc == nullptr || (n > 0 && x == nullptr))) return WQ_E_NULL;
+    if (n == 0 || K == 0) return WQ_OK;
+    cudaError_t e = wq::launch_channel_abs_sum(x, n, K, ldx, acc, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_awq_pre_scale_f32(const float* mag, int64_t K, float alpha, float* pre, void* stream) {
+    if (K < 0) return WQ_E_NEG_DIM;
+    if (K > 0 && ((alpha != 0.0f && mag == nullptr) || pre == nullptr)) return WQ_E_NULL;
+    cudaError_t e = wq::launch_pre_scale(mag, K, alpha, pre, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+size_t wq_sq_err_workspace_bytes(void) { return wq::sq_err_workspace_bytes(); }
+
+int wq_sq_err_sum_f64(const float* a, const float* b, int64_t n, double* out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    if (n < 0) return WQ_E_NEG_DIM;
+    if (out == nullptr || (n > 0 && (a == nullptr || b == nullptr))) return WQ_E_NULL;
+    if (workspace == nullptr || workspace_bytes < wq::sq_err_workspace_bytes()) return WQ_E_WORKSPACE;
+    cudaError_t e = wq::launch_sq_err_sum(a, b, n, out, workspace, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
 }  // extern "C"

@@ -83,6 +83,13 @@ cudaError_t launch_gather_permute(const float* src, int64_t P, int64_t B, int64_
 cudaError_t launch_widen_f16_f32(const uint16_t* src, float* dst, int64_t n, cudaStream_t s);
 cudaError_t launch_narrow_f32_f16(const float* src, uint16_t* dst, int64_t n, cudaStream_t s);
 
+// --- AWQ search reductions (awq.cu) ----------------------------------------
+cudaError_t launch_channel_abs_sum(const float* x, int64_t n, int64_t K, int64_t ldx, double* acc, cudaStream_t s);
+cudaError_t launch_pre_scale(const float* mag, int64_t K, float alpha, float* pre, cudaStream_t s);
+size_t sq_err_workspace_bytes();
+cudaError_t launch_sq_err_sum(const float* a, const float* b, int64_t n, double* out, void* workspace,
+                              cudaStream_t s);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
