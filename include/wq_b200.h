@@ -229,6 +229,32 @@ WQ_API int wq_sq_err_sum_f64(const float* a, const float* b, int64_t n, double* 
                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* GPTQ column sweep (src/ptqkit/gptq.py:86-191), fp64. The caller factors   */
+/* the damped inverse Hessian (gptq.py:44-71) and applies each block's       */
+/* update of the later columns as one GEMM (gptq.py:124-125); these are the  */
+/* per-row parts.                                                            */
+/* ------------------------------------------------------------------------ */
+/* Grid of quant.py:146-172 in fp64 over columns [c0, c1) of w (fp64 [rows,  */
+/* ld]): per row (per_tensor = 0; scale_out/zero_out[r * out_stride]) or for */
+/* the whole range of every row (per_tensor = 1; one value at [0]). The      */
+/* workspace (per_tensor only) holds wq_gptq_qparams_workspace_bytes(rows).   */
+WQ_API size_t wq_gptq_qparams_workspace_bytes(int64_t rows);
+WQ_API int wq_gptq_qparams_f64(const double* w, int64_t rows, int64_t ld, int64_t c0, int64_t c1,
+                               int bits, int symmetric, int per_tensor,
+                               double* scale_out, double* zero_out, int64_t out_stride,
+                               void* workspace, size_t workspace_bytes, void* stream);
+/* One block of _obs_block (gptq.py:86-125) without its last line: columns   */
+/* [s0, s0 + count) of every row of w are quantized left to right with the   */
+/* row's scale/zero (scale[r * qp_stride]; qp_stride 0 = one pair for all    */
+/* rows), each column's OBS error corrects the block's later columns with    */
+/* U = hinv (fp64 [K, ldh], upper Cholesky factor of the damped inverse), in */
+/* the reference's operation order. Writes int32 codes[r * ldc + s0 + i] and  */
+/* the errors err_block (fp64 [rows, count]); w is read only. count <= 128.   */
+WQ_API int wq_gptq_block_f64(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh,
+                             int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
+                             int bits, int32_t* codes, int64_t ldc, double* err_block, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */
 /* whose kernel runs on one CPU and splits rows across OpenMP threads        */
 /* (dequant_gemm.cpp:196-205). Each rank computes its rows of y; the         */

@@ -245,3 +245,111 @@ def awq_search(
         if mse < best_mse:
             best_alpha, best_mse, best = a, mse, r
     return {"alpha": best_alpha, "mse": mses, "pre_scale": pres, "rtn": best, "mag": mag}
+
+
+def _qparams64(block: np.ndarray, symmetric: bool, bits: int) -> tuple[np.ndarray, np.ndarray]:
+    """quant.py:146-172 on an fp64 [rows, cols] block; returns [rows] scale, zero."""
+    qmax = (1 << bits) - 1
+    if symmetric:
+        amax = np.abs(block).max(axis=1)
+        scale = np.where(amax > 0, (2 * amax) / qmax, 1.0)
+        return scale, np.full_like(scale, (qmax + 1) / 2.0)
+    xmin = np.minimum(block.min(axis=1), 0.0)
+    xmax = np.maximum(block.max(axis=1), 0.0)
+    deg = (xmin == 0) & (xmax == 0)
+    xmin = np.where(deg, -1.0, xmin)
+    xmax = np.where(deg, 1.0, xmax)
+    scale = (xmax - xmin) / qmax
+    scale = np.where(scale > 0, scale, 1.0)
+    zero = np.clip(np.rint(-xmin / scale), 0, qmax)
+    return scale, zero
+
+
+def gptq_factor(hessian: np.ndarray, percdamp: float) -> np.ndarray:
+    """Upper Cholesky factor of the damped inverse Hessian (src/ptqkit/gptq.py:44-71)."""
+    import scipy.linalg
+
+    h = 0.5 * (hessian + hessian.T)
+    dead = np.diag(h) == 0
+    if dead.any():
+        h = h.copy()
+        h[dead, :] = 0
+        h[:, dead] = 0
+        idx = np.arange(h.shape[0])[dead]
+        h[idx, idx] = 1
+    damp = percdamp * np.mean(np.diag(h))
+    if not np.isfinite(damp) or damp < 0:
+        damp = 0.0
+    h = h.copy()
+    h[np.diag_indices_from(h)] += damp
+    for _ in range(6):
+        try:
+            low = np.linalg.cholesky(h)
+            inv = scipy.linalg.cho_solve((low, True), np.eye(h.shape[0]))
+            return np.linalg.cholesky(inv).T
+        except np.linalg.LinAlgError:
+            h[np.diag_indices_from(h)] += np.mean(np.diag(h)) * 0.1 + 1e-6
+    raise RuntimeError("damped Hessian Cholesky failed")
+
+
+def gptq_quantize(
+    w: np.ndarray,
+    hessian: np.ndarray,
+    bits: int,
+    symmetric: bool,
+    group_size: int | None,
+    percdamp: float = 0.01,
+    blocksize: int = 128,
+    hinv: np.ndarray | None = None,
+) -> dict[str, np.ndarray | int]:
+    """src/ptqkit/gptq.py:86-191 restated in numpy fp64 (the OBS sweep column by
+    column, as _obs_block). ``hinv`` replaces the factorization when given."""
+    work = np.array(w, dtype=np.float64)
+    h = np.asarray(hessian, dtype=np.float64)
+    dead = np.diag(h) == 0
+    work[:, dead] = 0
+    u = gptq_factor(h, percdamp) if hinv is None else np.asarray(hinv, dtype=np.float64)
+    out, inn = work.shape
+    qmax = (1 << bits) - 1
+    codes = np.zeros((out, inn), dtype=np.int32)
+
+    def obs_block(sc: np.ndarray, zz: np.ndarray, start: int, end: int) -> None:
+        block = work[:, start:end].copy()
+        err_block = np.zeros_like(block)
+        for i in range(end - start):
+            col = block[:, i].copy()
+            d = u[start + i, start + i]
+            q = np.clip(np.rint(col / sc) + zz, 0, qmax)
+            deq = sc * (q - zz)
+            codes[:, start + i] = q.astype(np.int32)
+            err = (col - deq) / max(d, 1e-8)
+            if not np.isfinite(err).all():
+                err = np.zeros_like(col)
+            block[:, i:] = block[:, i:] - err[:, None] * u[start + i, start + i:end][None, :]
+            err_block[:, i] = err
+        if end < inn:
+            work[:, end:] = work[:, end:] - err_block @ u[start:end, end:]
+
+    if group_size is not None and group_size > 0:
+        scs, zzs = [], []
+        for start in range(0, inn, group_size):
+            end = min(start + group_size, inn)
+            sc, zz = _qparams64(work[:, start:end], symmetric, bits)
+            obs_block(sc, zz, start, end)
+            scs.append(sc)
+            zzs.append(zz)
+        scales, zeros, stored = np.stack(scs, axis=1), np.stack(zzs, axis=1), group_size
+    else:
+        if group_size == 0:
+            sc, zz = _qparams64(work.reshape(1, -1), symmetric, bits)
+            scales, zeros = sc.reshape(1, 1), zz.reshape(1, 1)
+            scv, zzv = np.full(out, sc[0]), np.full(out, zz[0])
+        else:
+            sc, zz = _qparams64(work, symmetric, bits)
+            scales, zeros = sc.reshape(-1, 1), zz.reshape(-1, 1)
+            scv, zzv = sc, zz
+        for start in range(0, inn, blocksize):
+            obs_block(scv, zzv, start, min(start + blocksize, inn))
+        stored = inn
+    return {"codes": codes, "scales": scales.astype(np.float32), "zeros": zeros.astype(np.float32),
+            "group_size": stored, "hinv": u}

@@ -152,10 +152,3 @@ def test_quantize_model_awq_tiny_mlp(wq, cuda, sequential: bool, kernel: bool) -
     x = torch.cat(batches).cpu().numpy()
     r = oracle.awq_search(w1, x, 4, True, 8, config.awq_alphas)
     assert model.fc1.awq_alpha == r["alpha"]
-
-
-def test_quantize_model_gptq_not_built(wq, cuda) -> None:
-    model = Tiny().to(cuda)
-    config = wq.QuantConfig(bits=4, symmetric=True, group_size=8, method=wq.Method.GPTQ)
-    with pytest.raises(NotImplementedError):
-        wq.quantize_model(model, config, [torch.randn(4, 16).to(cuda)])

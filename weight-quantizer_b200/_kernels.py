@@ -70,6 +70,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_awq_pre_scale_f32": (_int, [_vp, _i64, ctypes.c_float, _vp, _vp]),
     "wq_sq_err_workspace_bytes": (_sz, []),
     "wq_sq_err_sum_f64": (_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "wq_gptq_qparams_workspace_bytes": (_sz, [_i64]),
+    "wq_gptq_qparams_f64": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _i64, _vp, _sz, _vp]),
+    "wq_gptq_block_f64": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _vp, _i64, _int, _vp, _i64, _vp, _vp]),
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
@@ -542,3 +545,38 @@ def sq_err_sum(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     out = torch.empty((), dtype=torch.float64, device=dev)
     _check(lib.wq_sq_err_sum_f64(_ptr(a), _ptr(b), int(a.numel()), _ptr(out), _ptr(ws), ws_bytes, _stream(dev)))
     return out
+
+
+# ---- GPTQ column sweep (src/ptqkit/gptq.py:86-191) ---------------------------
+
+
+def gptq_qparams(w: torch.Tensor, c0: int, c1: int, bits: int, symmetric: bool, per_tensor: bool,
+                 scale_out: torch.Tensor, zero_out: torch.Tensor, out_stride: int) -> None:
+    """quant.py:146-172 in fp64 over columns [c0, c1) of w, per row (into
+    scale_out[r * out_stride]) or over the whole range (into [0])."""
+    dev = _cuda_device([w, scale_out, zero_out])
+    if w.dtype != torch.float64 or w.stride(1) != 1:
+        raise ValueError("w must be an fp64 matrix with unit column stride")
+    lib = library()
+    rows = int(w.shape[0])
+    ws_bytes = int(lib.wq_gptq_qparams_workspace_bytes(rows)) if per_tensor else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    _check(lib.wq_gptq_qparams_f64(_ptr(w), rows, int(w.stride(0)), int(c0), int(c1), int(bits), int(symmetric),
+                                   int(per_tensor), _ptr(scale_out), _ptr(zero_out), int(out_stride), _ptr(ws),
+                                   ws_bytes, _stream(dev)))
+
+
+def gptq_block(w: torch.Tensor, hinv: torch.Tensor, s0: int, count: int, scale: torch.Tensor,
+               zero: torch.Tensor, qp_stride: int, bits: int, codes: torch.Tensor, err_block: torch.Tensor) -> None:
+    """_obs_block's column sweep over [s0, s0 + count) (gptq.py:86-121): writes
+    codes[:, s0:s0 + count] and the OBS errors into err_block [rows, count]."""
+    dev = _cuda_device([w, hinv, scale, zero, codes, err_block])
+    for t in (w, hinv, scale, zero, err_block):
+        if t.dtype != torch.float64:
+            raise ValueError("GPTQ operands are fp64")
+    if codes.dtype != torch.int32 or not err_block.is_contiguous() or w.stride(1) != 1 or hinv.stride(1) != 1:
+        raise ValueError("codes must be int32; w, hinv row-major; err_block contiguous")
+    _check(library().wq_gptq_block_f64(_ptr(w), int(w.shape[0]), int(w.stride(0)), _ptr(hinv), int(hinv.stride(0)),
+                                       int(s0), int(count), _ptr(scale), _ptr(zero), int(qp_stride), int(bits),
+                                       _ptr(codes), int(codes.stride(0)), _ptr(err_block), _stream(dev)))
+

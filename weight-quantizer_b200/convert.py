@@ -1,10 +1,11 @@
 """Replace nn.Linear and GPT-2 Conv1D modules with QuantizedLinear on the GPU.
 
 Mirror of ptqkit's ``quantize_model`` (src/ptqkit/convert.py:236-293) for the
-RTN and AWQ methods, with the model's parameters on a CUDA device instead of
+RTN, AWQ and GPTQ methods, with the model's parameters on a CUDA device instead of
 the CPU (ptqkit's ``_check_cpu``, convert.py:122-126, becomes a CUDA check):
 every target weight is quantized by the GPU RTN kernel (bit-exact with
-ptqkit's quantize_weight) or by the GPU AWQ search (``awq.awq_quantize``), and
+ptqkit's quantize_weight), the GPU AWQ search (``awq.awq_quantize``) or the
+GPU GPTQ sweep (``gptq.gptq_quantize``), and
 the module is replaced by a QuantizedLinear whose ``impl="kernel"`` forward
 runs the dequant-GEMM with the bias added in the kernel's epilogue.
 
@@ -12,8 +13,9 @@ AWQ calibration follows convert.py:26-254: forward pre-hooks collect each
 target's inputs, either as running statistics over one pass of the
 calibration set (channel |x| sums in fp64 and the first 2048 rows,
 ActivationStats) or, with ``sequential=True``, as every input row of one
-target at a time with the earlier targets already replaced. GPTQ (its Hessian
-and column sweep) is not part of this build and raises NotImplementedError.
+target at a time with the earlier targets already replaced. GPTQ takes its
+Hessian X^T X / n from the same capture (an fp64 Gram matrix on the device)
+and runs ``gptq.gptq_quantize``.
 
 Conv1D stores its weight as [in, out] and computes x @ W; the quantizer stores
 [out, in] for both layouts, so the forward is always x @ W_hat^T + bias
@@ -30,6 +32,7 @@ from torch import nn
 
 from . import _kernels
 from .awq import awq_quantize, channel_mean_abs
+from .gptq import gptq_quantize
 from .linear import QuantizedLinear
 from .quant import Method, QuantConfig, QuantizedWeight, quantize_weight
 
@@ -39,15 +42,22 @@ _SAMPLE_ROWS = 2048
 
 class ActivationStats:
     """Running statistics of one target's inputs (convert.py:35-70), on the device:
+    the fp64 Gram matrix X^T X (for GPTQ's Hessian; kept only when asked for),
     the fp64 sum of |x| per input channel, the row count and the first 2048 rows."""
 
-    def __init__(self) -> None:
+    def __init__(self, gram: bool = True) -> None:
+        self.keep_gram = gram
+        self.xtx: torch.Tensor | None = None
         self.abs_sum: torch.Tensor | None = None
         self.count: int = 0
         self.sample: torch.Tensor | None = None
 
     def update(self, hidden: torch.Tensor) -> None:
         x = hidden.detach().reshape(-1, hidden.shape[-1]).to(dtype=torch.float32)
+        if self.keep_gram:
+            x64 = x.double()
+            gram = x64.transpose(0, 1) @ x64
+            self.xtx = gram if self.xtx is None else self.xtx + gram
         self.abs_sum = _kernels.channel_abs_sum(x, self.abs_sum)
         self.count += int(x.shape[0])
         if self.sample is None:
@@ -55,6 +65,11 @@ class ActivationStats:
         elif int(self.sample.shape[0]) < _SAMPLE_ROWS:
             need = _SAMPLE_ROWS - int(self.sample.shape[0])
             self.sample = torch.cat((self.sample, x[:need].clone()), dim=0)
+
+    def hessian(self) -> torch.Tensor:
+        if self.xtx is None or self.count == 0:
+            raise RuntimeError("no calibration rows")
+        return self.xtx / self.count
 
     def mean_abs(self) -> torch.Tensor:
         if self.abs_sum is None or self.count == 0:
@@ -142,9 +157,9 @@ def _as_batches(batches: Sequence[Batch]) -> list[Batch]:
 
 
 def _capture_all(model: nn.Module, names: list[tuple[str, nn.Module]],
-                 batches: Sequence[Batch]) -> dict[str, ActivationStats]:
+                 batches: Sequence[Batch], gram: bool = True) -> dict[str, ActivationStats]:
     """One pass of the calibration set with a statistics hook on every target (convert.py:140-162)."""
-    stats = {name: ActivationStats() for name, _ in names}
+    stats = {name: ActivationStats(gram) for name, _ in names}
     handles = []
     for name, module in names:
 
@@ -196,6 +211,16 @@ def _quantize_one(weight: torch.Tensor, config: QuantConfig, stats: ActivationSt
     """RTN, or AWQ from captured statistics or rows (convert.py:206-233)."""
     if config.method is Method.RTN:
         return quantize_weight(weight, config), None
+    if config.method is Method.GPTQ:
+        if stats is None and rows is None:
+            raise ValueError("GPTQ requires calibration activations")
+        if rows is not None and stats is None:
+            r64 = rows.double()
+            hessian = r64.transpose(0, 1) @ r64 / float(rows.shape[0])
+        else:
+            assert stats is not None
+            hessian = stats.hessian()
+        return gptq_quantize(weight, hessian, config), None
     if config.method is Method.AWQ:
         if rows is None and stats is None:
             raise ValueError("AWQ requires calibration activations")
@@ -207,7 +232,7 @@ def _quantize_one(weight: torch.Tensor, config: QuantConfig, stats: ActivationSt
             sample = rows[:_SAMPLE_ROWS]
             mean_abs = channel_mean_abs(rows)
         return awq_quantize(weight, sample, config, mean_abs=mean_abs)
-    raise NotImplementedError(f"{config.method.value} is not part of this build; use RTN or AWQ")
+    raise ValueError(f"unknown method {config.method}")
 
 
 def quantize_model(
@@ -231,8 +256,6 @@ def quantize_model(
     targets = iter_targets(model)
     if config.method is not Method.RTN and calibration_batches is None:
         raise ValueError(f"{config.method.value} requires calibration_batches")
-    if config.method is Method.GPTQ:
-        raise NotImplementedError("gptq is not part of this build; use RTN or AWQ")
     batches = [] if calibration_batches is None else _as_batches(calibration_batches)
 
     with torch.inference_mode():
@@ -244,7 +267,7 @@ def quantize_model(
                 if sequential:
                     rows = _capture_one(model, "root", module, batches)
                 else:
-                    stats = _capture_all(model, [("root", module)], batches)["root"]
+                    stats = _capture_all(model, [("root", module)], batches, config.method is Method.GPTQ)["root"]
             qw, alpha = _quantize_one(weight_out_in(module), config, stats, rows)
             layer = _module_from(qw, module, kernel=kernel, alpha=alpha)
             if cache_weights:
@@ -253,7 +276,7 @@ def quantize_model(
         if config.method is Method.RTN or not sequential:
             stats_map: dict[str, ActivationStats] | None = None
             if config.method is not Method.RTN:
-                stats_map = _capture_all(model, targets, batches)
+                stats_map = _capture_all(model, targets, batches, config.method is Method.GPTQ)
             for name, module in targets:
                 stats = None if stats_map is None else stats_map[name]
                 qw, alpha = _quantize_one(weight_out_in(module), config, stats, None)

@@ -440,4 +440,38 @@ int wq_sq_err_sum_f64(const float* a, const float* b, int64_t n, double* out, vo
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 
+size_t wq_gptq_qparams_workspace_bytes(int64_t rows) { return rows > 0 ? wq::gptq_qparams_workspace_bytes(rows) : 0; }
+
+int wq_gptq_qparams_f64(const double* w, int64_t rows, int64_t ld, int64_t c0, int64_t c1, int bits, int symmetric,
+                        int per_tensor, double* scale_out, double* zero_out, int64_t out_stride, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    if (rows < 0 || c0 < 0 || c1 < c0 || out_stride < 0) return WQ_E_NEG_DIM;
+    if (bits != 4 && bits != 8) return WQ_E_BITS;
+    if (ld < c1) return WQ_E_LD;
+    if (rows == 0) return WQ_OK;
+    if (w == nullptr || scale_out == nullptr || zero_out == nullptr) return WQ_E_NULL;
+    if (per_tensor && (workspace == nullptr || workspace_bytes < wq::gptq_qparams_workspace_bytes(rows)))
+        return WQ_E_WORKSPACE;
+    cudaError_t e = wq::launch_gptq_qparams(w, rows, ld, c0, c1, bits, symmetric, per_tensor, scale_out, zero_out,
+                                            out_stride, static_cast<double*>(workspace),
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_gptq_block_f64(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh, int64_t s0,
+                      int count, const double* scale, const double* zero, int64_t qp_stride, int bits,
+                      int32_t* codes, int64_t ldc, double* err_block, void* stream) {
+    if (rows < 0 || s0 < 0 || count < 0 || qp_stride < 0) return WQ_E_NEG_DIM;
+    if (bits != 4 && bits != 8) return WQ_E_BITS;
+    if (count > wq::gptq_max_block() || rows > kMaxDim) return WQ_E_TOO_LARGE;
+    if (ld < s0 + count || ldh < s0 + count || ldc < s0 + count) return WQ_E_LD;
+    if (rows == 0 || count == 0) return WQ_OK;
+    if (w == nullptr || hinv == nullptr || scale == nullptr || zero == nullptr || codes == nullptr ||
+        err_block == nullptr)
+        return WQ_E_NULL;
+    cudaError_t e = wq::launch_gptq_block(w, rows, ld, hinv, ldh, s0, count, scale, zero, qp_stride, bits, codes, ldc,
+                                          err_block, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
 }  // extern "C"

@@ -90,6 +90,16 @@ size_t sq_err_workspace_bytes();
 cudaError_t launch_sq_err_sum(const float* a, const float* b, int64_t n, double* out, void* workspace,
                               cudaStream_t s);
 
+// --- GPTQ column sweep (gptq.cu) ----------------------------------------------
+size_t gptq_qparams_workspace_bytes(int64_t rows);
+cudaError_t launch_gptq_qparams(const double* w, int64_t rows, int64_t ld, int64_t c0, int64_t c1, int bits,
+                                int symmetric, int per_tensor, double* scale_out, double* zero_out,
+                                int64_t out_stride, double* workspace, cudaStream_t s);
+int gptq_max_block();
+cudaError_t launch_gptq_block(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh,
+                              int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
+                              int bits, int32_t* codes, int64_t ldc, double* err_block, cudaStream_t s);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
