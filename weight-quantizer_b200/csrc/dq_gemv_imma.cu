@@ -1,5 +1,5 @@
-// K1i — int4 decode dequant-GEMM for batches 1-2 on the integer tensor-core
-// path (mma.sync u8 x s8 -> s32).
+// K1i — int4 decode dequant-GEMM for batches 1-2 (3-4 as two launches) on the
+// integer tensor-core path (mma.sync u8 x s8 -> s32).
 //
 // Same math as ptqkit's CPU kernel (src/ptqkit/csrc/dequant_gemm.cpp:57-218,
 // run_gemm / dequant_row / dots_into), y[b,m] = sum_g scale[m,g] * sum_{k in g}
@@ -16,35 +16,38 @@
 //     in registers: a 32-bit word of codes 8c..8c+7 gives the even codes
 //     (w & 0x0F0F0F0F) and the odd codes ((w >> 4) & 0x0F0F0F0F), 3 ALU
 //     operations per 8 codes. One mma.sync.m16n8k32 multiplies 16 rows x 32
-//     codes by the 32 x 8 digit matrix whose columns are the three limbs of
-//     batch row 0 (columns 0-2) and of batch row 1 (columns 3-5); columns 6-7
-//     are zero. Products and s32 accumulators are exact, so
-//     C[m, 3b+l] = sum_k q[m,k] d_lk(b).
-//   * Per fold block and row: sum_k q x'_b = 2^(e-22) sum_l 256^l C[m, 3b+l],
+//     codes by the 32 x 8 digit matrix whose column 4b + l (l < 3) is limb l
+//     of batch row b; columns 4b + 3 are empty. Products and s32 accumulators
+//     are exact, so C[m, 4b+l] = sum_k q[m,k] d_lk(b).
+//   * Per fold block and row: sum_k q x'_b = 2^(e-22) sum_l 256^l C[m, 4b+l],
 //     and the zero point enters as zero * sum_k X_k (the integer sum of the
-//     same block). Each column is folded into an fp32 accumulator with the
-//     row's scale; the lanes holding columns 6-7 carry the zero-point terms.
+//     same block). A lane's two C columns belong to one batch row: limbs 0-1
+//     (combined as C0 + 256 C1, exact in s32), or limb 2 and the empty
+//     column, in which that lane folds the zero-point term. Each lane folds
+//     into one fp32 accumulator per row with the row's scale.
 //
 // The integer MMA runs at the full legacy tensor rate on sm_100 (the 4-bit
 // u4 x s4 form does not: it is about 20x slower there), and one MMA covers
 // 512 codes with ~11 ALU instructions, a small fraction of a SIMT
 // multiply-add loop's cost, which leaves the kernel bound by the weight stream.
 //
-// Mapping. 8 warps per CTA, one CTA per SM (persistent). Warp w owns the fold
-// blocks [w*nfb/8, (w+1)*nfb/8) of every row and keeps their digit fragments
-// (the MMA's B operand) in registers for the whole launch: lane (g, t) =
-// (lane/4, lane%4) holds column g of the codes that thread-in-group t supplies.
-// Rows stream past 16 at a time: one warp per stage issues one bulk
-// asynchronous copy (cp.async.bulk) per row of codes and per row of the
-// scale/zero tables into a ring of shared-memory stages, completing on an
-// mbarrier. Shared-memory rows are padded so that the fragment loads (16 or
-// 8 bytes per lane) are free of bank conflicts. Each warp folds its slice's
-// accumulators, reduces the four column pairs with two shuffles and leaves
-// one partial per row and batch row in shared memory; a rotating warp adds
-// the 8 partials in a fixed order (deterministic, no atomics), writes y and
-// refills the stage. Every mbarrier wait is bounded; on expiry the kernel
-// sets bit 0 of the library's fault word and runs to completion without
-// waiting again.
+// Mapping. 8 multiply warps and one producer warp per CTA, one CTA per SM
+// (persistent). Multiply warp w owns the fold blocks [w*nfb/8, (w+1)*nfb/8)
+// of every row and keeps their digit fragments (the MMA's B operand) in
+// registers for the whole launch: lane (g, t) = (lane/4, lane%4) holds column
+// g of the codes that thread-in-group t supplies. Rows stream past in row
+// blocks of 8-16 rows (chosen so that the last wave is full; the MMA's other
+// rows are ignored): the producer issues one bulk asynchronous copy
+// (cp.async.bulk) per row of codes, and per table or per table row, into a
+// ring of shared-memory stages, completing on an mbarrier. Shared-memory rows
+// are padded so that the fragment loads (16 or 8 bytes per lane) are free of
+// bank conflicts. Each multiply warp folds its slice's accumulators, adds the
+// lanes of one batch row with shuffles and leaves one partial per row and
+// batch row in shared memory; the producer adds the 8 partials in a fixed
+// order (deterministic, no atomics), writes y and refills the stage. The x'
+// loads are issued before the weight stream so that they do not queue behind
+// it. Every mbarrier wait is bounded; on expiry the kernel sets bit 0 of the
+// library's fault word and runs to completion without waiting again.
 #include <atomic>
 
 #include "common.cuh"
