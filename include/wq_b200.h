@@ -78,12 +78,18 @@ WQ_API const char* wq_last_cuda_error(void);
 
 /* Fault word of the current device. Bit 0: a bounded wait on a pipeline
  * barrier expired (the launch then completed without waiting again, and its
- * output is not valid). Bit 1: the tensor-core path met a zero point that is
- * not an integer in [0, 1023] (its (code - zero) was rounded to fp16, so that
- * output is less accurate than the stated tolerance). Synchronizes with the
- * device. `reset` nonzero clears the word after reading it. No counterpart in
- * the reference, whose CPU kernel has no asynchronous waits. */
+ * output is not valid). Other bits are reserved and stay 0. Synchronizes with
+ * the device. `reset` nonzero clears the word after reading it. No
+ * counterpart in the reference, whose CPU kernel has no asynchronous waits. */
 WQ_API int wq_fault_status(int reset, uint32_t* out);
+
+/* Self-test of the fault reporting: one thread initializes a shared-memory
+ * barrier that nothing ever arrives on and waits for it with the library's
+ * bounded wait, giving up after `max_polls` polls (1 <= max_polls <= 2^22).
+ * When the wait gives up, bit 0 of the fault word is set, exactly as when a
+ * pipeline wait of a real kernel expires; nothing else is touched and no copy
+ * is in flight. Enqueued on `stream`. No counterpart in the reference. */
+WQ_API int wq_selftest_expired_wait(uint32_t max_polls, void* stream);
 
 /* Build/device facts, the counterpart of `_kernels.kernel_info()`
  * (dequant_gemm.cpp:302-315, which reports {"avx2", "openmp"}). */
@@ -136,7 +142,9 @@ WQ_API int wq_dequant_gemm_f32(const float* x, int64_t B, int64_t K,
  * device share the array and every call writes the scratch it reads before
  * reading it, but calls whose work overlaps on the GPU race on it. The first
  * call on each device resolves the array's device address
- * (cudaGetSymbolAddress); make it before capturing a stream. */
+ * (cudaGetSymbolAddress); make it before capturing a stream. The address is
+ * kept per device and CUDA context, so after a cudaDeviceReset the next call
+ * resolves it again. */
 WQ_API int wq_dequant_gemm_f32_noalloc(const float* x, int64_t B, int64_t K,
                                        const uint8_t* q, int64_t M, int64_t q_cols,
                                        const float* scales, int64_t scale_rows, int64_t groups,

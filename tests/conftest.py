@@ -19,6 +19,9 @@ import numpy as np
 import pytest
 
 REPO = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+# every dequant-GEMM call in the tests reads the kernels' fault word and raises
+# if a bounded wait expired (checked mode of weight-quantizer_b200._kernels)
+os.environ.setdefault("WQ_CHECK_FAULTS", "1")
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 GOLDEN = os.path.join(REPO, "tests", "golden")

@@ -190,3 +190,55 @@ def test_workloads_vs_oracle(wq, orc, cuda, wname: str) -> None:
                 rows = torch.randperm(b, generator=sample)[:64]
                 ref = _oracle_y(orc, qw, x[rows])
                 assert_close_y(got[rows].numpy(), ref, f"{wname}/{layer.name} b{b} sampled rows")
+
+
+@pytest.mark.parametrize("batch", [5, 64, 4096])
+def test_fractional_zero_points_vs_oracle(wq, orc, cuda, batch: int) -> None:
+    """ptqkit's operator takes any fp32 zero point (dequant_gemm.cpp:73-86
+    computes (code - zero) * scale in fp32). The tensor-core path builds A from
+    the zero's integer part and subtracts the fractional rest times the group's
+    sum of x' in its epilogue. Rows mix integer, fractional, negative and
+    above-range zeros, so that some warps take the correction and some do not;
+    per-tensor tables and a channel scale are covered too. Zeros far outside
+    the code range make y a small difference of large terms, so that case uses
+    positive activations (a well-conditioned sum; with mixed signs any two fp32
+    summation orders differ by more than the tolerance there)."""
+    g = torch.Generator().manual_seed(700 + batch)
+    cases = ((4, 300, 1024, 128, False, False), (8, 256, 768, 64, True, False), (4, 160, 512, 512, False, False),
+             (4, 160, 512, 128, False, True))
+    for bits, M, K, group, pre, far in cases:
+        qw = _rand_layer(wq, g, M, K, bits, False, group, pre)
+        z = qw.zeros.cpu().clone()
+        rows = z.shape[0]
+        frac = torch.rand(z.shape, generator=g) - 0.5
+        z[rows // 3:] += frac[rows // 3:]                       # fractional from row M/3 on
+        z[: rows // 8] = torch.tensor(-2.75)                    # negative, fractional
+        x = torch.randn(batch, K, generator=g)
+        if far:
+            z[rows // 8: rows // 6] = torch.tensor(1500.25)     # beyond the integer part's [0, 1023]
+            x = x.abs() + 0.1
+        ch = None if qw.channel_scale is None else qw.channel_scale
+        got = wq._kernels.dequant_gemm(x.to(cuda), qw.codes, qw.scales, z.to(cuda), ch, qw.group_size, bits)
+        ref = orc.dequant_gemm(x.numpy(), qw.codes.cpu().numpy(), qw.scales.cpu().numpy(), z.numpy(),
+                               None if ch is None else ch.cpu().numpy(), qw.group_size, bits)
+        assert_close_y(got.cpu().numpy(), ref, f"bits{bits} {M}x{K} g{group} b{batch} fractional zeros")
+        assert wq._kernels.fault_status() == 0
+    # per-tensor table with one fractional zero for every row
+    qw = _rand_layer(wq, g, 200, 640, 8, False, 0)
+    z = qw.zeros.cpu() + 0.375
+    x = torch.randn(batch, 640, generator=g)
+    got = wq._kernels.dequant_gemm(x.to(cuda), qw.codes, qw.scales, z.to(cuda), None, qw.group_size, 8)
+    ref = orc.dequant_gemm(x.numpy(), qw.codes.cpu().numpy(), qw.scales.cpu().numpy(), z.numpy(), None,
+                           qw.group_size, 8)
+    assert_close_y(got.cpu().numpy(), ref, f"per-tensor fractional zero b{batch}")
+
+
+def test_integer_zero_points_unchanged_by_correction(wq, cuda) -> None:
+    """Adding an exact 0.0 to every zero point must not change a single bit:
+    warps whose zeros are all integers skip the fractional-zero term."""
+    g = torch.Generator().manual_seed(41)
+    qw = _rand_layer(wq, g, 512, 2048, 4, False, 128)
+    x = torch.randn(96, 2048, generator=g).to(cuda)
+    a = wq._kernels.dequant_gemm(x, qw.codes, qw.scales, qw.zeros, None, 128, 4)
+    b = wq._kernels.dequant_gemm(x, qw.codes, qw.scales, (qw.zeros + 0.0).contiguous(), None, 128, 4)
+    assert torch.equal(a, b)

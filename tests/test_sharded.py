@@ -121,3 +121,42 @@ def test_rank_that_never_joins_fails_the_collective(tmp_path) -> None:
     text = (tmp_path / "rank0.txt").read_text().split()
     assert text[0] == "raised", text
     assert float(text[-1]) < 30.0
+
+
+def _choose_worker(rank: int, world: int, port: int, fail: str, out_dir: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    sharded = importlib.import_module("weight-quantizer_b200.sharded")
+    calls: list[str] = []
+
+    def setup_local() -> str:
+        calls.append("local")
+        if fail == f"local{rank}":
+            raise RuntimeError("out of memory (injected on this rank)")
+        return "buffers"
+
+    def setup_collective(state: str) -> None:
+        assert state == "buffers"
+        calls.append("collective")
+        dist.barrier()   # the collective phase is a collective
+        if fail == f"collective{rank}":
+            raise RuntimeError("rendezvous failed (injected on this rank)")
+
+    ok = sharded.choose_collectively(setup_local, setup_collective, None, torch.device("cpu"))
+    dist.barrier()   # every rank is still in step after the choice
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{int(ok)} {','.join(calls)}")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail", ["none", "local1", "local0", "collective1"])
+def test_exchange_choice_is_collective(tmp_path, fail: str) -> None:
+    """A setup failure on one rank alone sends every rank to the same choice,
+    with every rank taking the same collectives (no rank left waiting)."""
+    world = 3
+    mp.spawn(_choose_worker, args=(world, _port(), fail, str(tmp_path)), nprocs=world, join=True)
+    results = [(tmp_path / f"r{r}.txt").read_text().split() for r in range(world)]
+    oks = {res[0] for res in results}
+    assert oks == {"1" if fail == "none" else "0"}, results
+    if fail.startswith("local"):
+        assert all(res[1] == "local" for res in results), results   # nobody entered the rendezvous

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_status_string": (ctypes.c_char_p, [_int]),
     "wq_last_cuda_error": (ctypes.c_char_p, []),
     "wq_fault_status": (_int, [_int, ctypes.POINTER(ctypes.c_uint32)]),
+    "wq_selftest_expired_wait": (_int, [ctypes.c_uint32, _vp]),
     "wq_kernel_info": (_int, [_int, _vp]),
     "wq_dequant_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
     "wq_dequant_gemm_f32": (
@@ -158,6 +159,38 @@ def fault_status(reset: bool = True) -> int:
     return int(v.value)
 
 
+# Checked mode: after every dequant-GEMM call, read (and clear) the fault word
+# and raise if a kernel set it. Reading it synchronizes the device, so it is
+# off by default; WQ_CHECK_FAULTS=1 in the environment or set_fault_check(True)
+# turns it on. Without it, fault_status() is the way to learn of an expired
+# wait (the kernels never hang on one: they stop waiting and finish).
+_fault_check = os.environ.get("WQ_CHECK_FAULTS", "") not in ("", "0")
+
+
+def set_fault_check(on: bool) -> bool:
+    """Turn checked mode on or off; returns the previous setting."""
+    global _fault_check
+    prev = _fault_check
+    _fault_check = bool(on)
+    return prev
+
+
+def _raise_on_fault() -> None:
+    v = fault_status(reset=True)
+    if v:
+        raise RuntimeError(
+            f"wq_b200: a kernel set the fault word ({v:#x}; bit 0 = a bounded pipeline wait expired), "
+            "so its output is not valid")
+
+
+def selftest_expired_wait(max_polls: int = 16, device: torch.device | None = None) -> None:
+    """Launch the library's self-test of fault reporting: a wait on a barrier
+    that nothing arrives on, given up after ``max_polls`` polls, which sets bit
+    0 of the fault word the way an expired pipeline wait does."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    _check(library().wq_selftest_expired_wait(int(max_polls), _stream(dev)))
+
+
 def kernel_info(device: int | None = None) -> dict[str, Any]:
     """Build and device facts (counterpart of ``_kernels.kernel_info``)."""
     if device is None:
@@ -255,6 +288,8 @@ def dequant_gemm(
             _stream(dev),
         )
     _check(status)
+    if _fault_check:
+        _raise_on_fault()
     return y
 
 
@@ -435,6 +470,8 @@ def dequant_gemm_multi(
         _stream(dev),
     )
     _check(status)
+    if _fault_check:
+        _raise_on_fault()
 
 
 def _bias_arg(bias: torch.Tensor | None, M: int, dev: torch.device) -> torch.Tensor | None:

@@ -30,20 +30,59 @@ int sm_count() {
 // Fault word of this library on every device that loads it.
 __device__ unsigned int g_wq_fault = 0;
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+    });
+    return fn;
+}
+
+// Looked up once per device and CUDA context: a cudaDeviceReset gives the
+// device a new context, and the address is then looked up again.
 unsigned int* fault_word() {
     static unsigned int* cached[64] = {nullptr};
+    static CUcontext cached_ctx[64] = {nullptr};
     static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    CtxGetCurrentFn get = ctx_get_current();
+    CUcontext ctx = nullptr;
+    if (get != nullptr && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (cached[dev] == nullptr) {
+    if (cached[dev] == nullptr || ctx == nullptr || cached_ctx[dev] != ctx) {
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_wq_fault) != cudaSuccess) return nullptr;
+        if (get != nullptr && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
         cached[dev] = static_cast<unsigned int*>(ptr);
+        cached_ctx[dev] = ctx;
     }
     return cached[dev];
 }
 
+namespace {
+
+// Waits on a shared-memory barrier that nothing arrives on, with the bounded
+// poll loop of the pipeline kernels (here with a caller-chosen limit), and
+// records the expiry in the fault word as they do.
+__global__ void selftest_expired_wait_kernel(uint32_t max_polls, unsigned int* fault) {
+    __shared__ __align__(8) unsigned long long bar_word;
+    const uint32_t bar = smem_addr(&bar_word);
+    mbar_init(bar, 1);
+    fence_mbarrier_init();
+    bool done = false;
+    for (uint32_t n = 0; n < max_polls && !done; ++n) done = mbar_try_wait(bar, 0);
+    if (!done) atomicOr(fault, 1u);
+}
+
+}  // namespace
 }  // namespace wq
 
 namespace {
@@ -123,12 +162,21 @@ int wq_fault_status(int reset, uint32_t* out) {
     return WQ_OK;
 }
 
+int wq_selftest_expired_wait(uint32_t max_polls, void* stream) {
+    if (max_polls < 1 || max_polls > wq::kMaxPolls) return WQ_E_TOO_LARGE;
+    unsigned int* fault = wq::fault_word();
+    if (fault == nullptr) return cuda_fail(cudaErrorInvalidDevicePointer);
+    wq::selftest_expired_wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(max_polls, fault);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
 size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
     (void)M;
     if (B <= 0 || K <= 0 || group_size <= 0 || (bits != 4 && bits != 8)) return 0;
     if (B <= wq::kGemvMaxBatch) return wq::gemv_workspace_bytes(B, K, bits);
     const bool single_group = group_size >= K;
-    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, K);
+    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, K, group_size);
     return 0;
 }
 
@@ -212,7 +260,7 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
         fan_out();
         e = wq::launch_gemv(p, workspace, s);
     } else if (wq::tc_supported(p)) {
-        const size_t need = wq::tc_workspace_bytes(B, K);
+        const size_t need = wq::tc_workspace_bytes(B, K, group_size);
         if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
         if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
         fan_out();

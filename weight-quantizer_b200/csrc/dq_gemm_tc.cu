@@ -4,13 +4,20 @@
 // batched inputs. The contraction runs on the 5th-generation tensor cores with
 // fp32 accuracy from fp16 operands:
 //
-//   * A = (q - zero) for one 128-row weight tile. Every code minus an integral
-//     zero point is an integer of magnitude <= 255, exact in fp16. Dequant
-//     warps build A from TMA-loaded packed codes (int4: LOP3 with the fp16
-//     exponent 0x6400 gives 1024 + code, HSUB2 of 1024 + zero gives the exact
-//     difference) and write it straight into tensor memory with tcgen05.st
-//     (lane = weight row, two fp16 per column), two 64-wide K tiles per A
-//     stage; the MMA reads A from tensor memory.
+//   * A = (q - zi) for one 128-row weight tile, zi = clamp(rint(zero), 0,
+//     1023): a code minus an integer in [0, 1023] is an integer of magnitude
+//     <= 1023, exact in fp16. Dequant warps build A from TMA-loaded packed
+//     codes (int4: LOP3 with the fp16 exponent 0x6400 gives 1024 + code,
+//     HSUB2 of 1024 + zi gives the exact difference) and write it straight
+//     into tensor memory with tcgen05.st (lane = weight row, two fp16 per
+//     column), two 64-wide K tiles per A stage; the MMA reads A from tensor
+//     memory. A zero point that is not such an integer (ptqkit's quantizers
+//     never produce one, but the operator accepts any fp32 zero) leaves
+//     dz = zero - zi, and the epilogue subtracts dz * sum_{k in g} x'_k * S_b
+//     (per batch row and group, summed by the prep kernel), so
+//     (q - zero) x' = (q - zi) x' - dz x' holds for every zero point. Warps
+//     whose 32 rows all have integer zero points skip that term, which keeps
+//     their results bit for bit what they were without it.
 //   * B = x' * S_b split into fp16 hi + lo planes by a prep kernel (x' = x *
 //     channel, S_b a per-batch-row power of two putting max|x'_b * S_b| in
 //     [2^13, 2^14)), so hi + lo carries ~22 significant bits of x'. The prep
@@ -100,6 +107,8 @@ struct TcParams {
     const float* scales;
     const float* zeros;
     const float* inv_s;   // [B] 2^-S_b
+    const float* xsum;    // [ngroups][bpad] sum over each group of x' * S_b
+    int bpad;             // batch rows of the padded planes (row stride of xsum)
     float* y;
     float* y_extra[7];    // further outputs with y's layout (peer-mapped on other GPUs)
     int n_extra;
@@ -179,18 +188,23 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// 8 int4 codes (one 32-bit word, k ascending) -> 8 fp16 values (code - zero)
+// The integer zero point A is built with: rint(zero) clamped to [0, 1023]
+// (1024 + zi is then exact in fp16; NaN maps to 0 and reaches y through the
+// epilogue's dz term, as it reaches the reference's (code - zero)).
+__device__ __forceinline__ float zero_int(float z) { return fminf(fmaxf(rintf(z), 0.0f), 1023.0f); }
+
+// 8 int4 codes (one 32-bit word, k ascending) -> 8 fp16 values (code - zi)
 // in the order the nibble masks produce them, k0 k4 k1 k5 k2 k6 k3 k7; the
 // prep kernel stores the x' planes of int4 layers in the same order inside
 // every group of 8, so the products pair up without a byte shuffle.
-// zz = half2(1024 + zero) twice.
+// zz = half2(1024 + zi) twice.
 __device__ __forceinline__ uint4 dq8_int4(uint32_t w, uint32_t zz) {
     return make_uint4(hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), zz),          // k0, k4
                       hsub2_u32(lop3_and_or(w >> 4, 0x000F000Fu, 0x64006400u), zz),     // k1, k5
                       hsub2_u32(lop3_and_or(w >> 8, 0x000F000Fu, 0x64006400u), zz),     // k2, k6
                       hsub2_u32(lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u), zz));   // k3, k7
 }
-// 8 int8 codes (two words) -> 8 fp16 (code - zero)
+// 8 int8 codes (two words) -> 8 fp16 (code - zi)
 __device__ __forceinline__ uint4 dq8_int8(uint32_t a, uint32_t b, uint32_t zz) {
     const uint32_t e = 0x64646464u;
     return make_uint4(hsub2_u32(__byte_perm(a, e, 0x4140), zz), hsub2_u32(__byte_perm(a, e, 0x4342), zz),
@@ -491,7 +505,6 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         const int64_t srow = p.scale_rows == 1 ? 0 : m;
         const uint32_t swz = (uint32_t)(r & 7);
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        bool inexact = false;
         // Zero points of groups g + 1 .. g + 4 are in flight while group g is
         // processed: every thread reads its own row, so these loads are not
         // coalesced and take longer than a few K tiles under load.
@@ -525,10 +538,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                   const int t = kTilesPerA * ja + h;
                   if (t < p.KT) {
                     const int kin = kTilesPerA * js + h;   // K tile inside the codes stage
-                    const float z = z_cur;
-                    const float zb = 1024.0f + z;
-                    const __half zh = __float2half_rn(zb);
-                    if (__half2float(zh) != zb || !(z >= 0.0f && z <= 1023.0f)) inexact = true;
+                    const __half zh = __float2half_rn(1024.0f + zero_int(z_cur));   // exact
                     const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
                     uint32_t a[32];
                     if constexpr (BITS == 4) {
@@ -582,7 +592,6 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                 cph ^= 1u;
             }
         }
-        if (inexact) atomicOr(p.fault, 2u);
     } else {
         set_regs<C::REGS_EPI, C::LAUNCH_REGS>();
         // ---- epilogue: thread owns row r of the tile, all BN columns -----------
@@ -600,6 +609,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         float sc_n3 = p.ngroups > 3 ? __ldg(srow_p + 3) : 0.0f;
         float sc_n4 = p.ngroups > 4 ? __ldg(srow_p + 4) : 0.0f;
         float sc = __ldg(srow_p);
+        // zero points of groups g + 1, g + 2 in flight, for the dz term
+        const float* zrow_p = p.zeros + srow * p.groups;
+        float zc = __ldg(zrow_p);
+        float z_n1 = p.ngroups > 1 ? __ldg(zrow_p + 1) : 0.0f;
+        float z_n2 = p.ngroups > 2 ? __ldg(zrow_p + 2) : 0.0f;
         for (int g = 0; g < p.ngroups; ++g) {
             const int buf = g & 1, use = g >> 1;
             wait_warp(acc_full(buf), (uint32_t)(use & 1));
@@ -627,6 +641,24 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty(buf));
+            // fractional zero points: acc -= scale * dz * sum_{k in g} x' S_b
+            // (rows with dz = 0 add 0 * sum, which leaves acc unchanged)
+            const float dz = zc - zero_int(zc);
+            if (__any_sync(0xffffffffu, dz != 0.0f)) {
+                const float cz = -(sc * dz);
+                const float4* xs = reinterpret_cast<const float4*>(p.xsum + (int64_t)g * p.bpad + n0);
+#pragma unroll
+                for (int i = 0; i < BN / 4; ++i) {
+                    const float4 v = __ldg(xs + i);
+                    acc[4 * i] = fmaf(cz, v.x, acc[4 * i]);
+                    acc[4 * i + 1] = fmaf(cz, v.y, acc[4 * i + 1]);
+                    acc[4 * i + 2] = fmaf(cz, v.z, acc[4 * i + 2]);
+                    acc[4 * i + 3] = fmaf(cz, v.w, acc[4 * i + 3]);
+                }
+            }
+            zc = z_n1;
+            z_n1 = z_n2;
+            if (g + 3 < p.ngroups) z_n2 = __ldg(zrow_p + g + 3);
             sc = sc_n1;
             sc_n1 = sc_n2;
             sc_n2 = sc_n3;
@@ -679,8 +711,11 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
 // Rows b >= B (padding of the last batch tile) are written as zeros. For
 // int4 layers (`nibble_order`) the 8 values of a chunk are stored in the order
 // k0 k4 k1 k5 k2 k6 k3 k7, matching the order the dequant warps produce A in.
+// Also xsum[g * bpad + b] = sum of x' * S_b over group g (gsz values; warp w
+// sums groups w, w + 8, ..., lanes strided then a butterfly: a fixed order).
 __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float* channel, int B, int K, int KT,
-                                                     int BN, bool nibble_order, unsigned char* planes, float* inv_s) {
+                                                     int BN, bool nibble_order, unsigned char* planes, float* inv_s,
+                                                     int gsz, int ngroups, int bpad, float* xsum) {
     __shared__ float red[8];
     const int b = blockIdx.x;
     const bool real = b < B;
@@ -733,6 +768,20 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float
         *reinterpret_cast<uint4*>(tile + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4*>(tile + plane_bytes + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int g = warp; g < ngroups; g += (int)(blockDim.x >> 5)) {
+        float acc = 0.0f;
+        if (real) {
+            const int k1 = min(K, (g + 1) * gsz);
+            for (int k = g * gsz + lane; k < k1; k += 32) {
+                float t = xb[k];
+                if (channel != nullptr) t = t * channel[k];
+                acc += t * S;
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) xsum[(int64_t)g * bpad + b] = acc;
+    }
 }
 
 // ---- host side ----------------------------------------------------------------
@@ -773,16 +822,27 @@ int64_t kt_of(int64_t K) { return (K + BK - 1) / BK; }
 int bn_of(int64_t B) { return B <= 32 ? 32 : (B <= 64 ? 64 : (B < 1024 ? 128 : 192)); }
 int64_t bpad_of(int64_t B) { const int bn = bn_of(B); return (B + bn - 1) / bn * bn; }
 
+// Groups as the kernel walks them: one per group_size (a multiple of BK),
+// or one for the whole row.
+int64_t ngroups_of(int64_t K, int group_size) { return group_size >= K ? 1 : (K + group_size - 1) / group_size; }
+int64_t round256(int64_t v) { return (v + 255) / 256 * 256; }
+
+// Workspace: [planes: bpad * KT * BK * 4 B][inv_s: B floats, padded to 256 B]
+// [xsum: ngroups * bpad floats]
 struct TcWorkspace {
     unsigned char* planes;
     float* inv_s;
+    float* xsum;
 };
 
-TcWorkspace carve(void* ws, int64_t B, int64_t K) {
+TcWorkspace carve(void* ws, int64_t B, int64_t K, int group_size) {
     unsigned char* p = static_cast<unsigned char*>(ws);
     TcWorkspace w;
+    const int64_t planes = bpad_of(B) * kt_of(K) * BK * 4;
     w.planes = p;
-    w.inv_s = reinterpret_cast<float*>(p + bpad_of(B) * kt_of(K) * BK * 4);
+    w.inv_s = reinterpret_cast<float*>(p + planes);
+    w.xsum = reinterpret_cast<float*>(p + planes + round256(B * 4));
+    (void)group_size;
     return w;
 }
 
@@ -798,6 +858,8 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.scales = g.scales;
     p.zeros = g.zeros;
     p.inv_s = w.inv_s;
+    p.xsum = w.xsum;
+    p.bpad = (int)bpad_of(g.B);
     p.y = g.y;
     p.n_extra = g.n_extra;
     p.y_all = g.y_all;
@@ -843,17 +905,20 @@ bool tc_supported(const GemmProblem& p) {
     return encode_fn() != nullptr;
 }
 
-size_t tc_workspace_bytes(int64_t B, int64_t K) {
-    // fp16 hi + lo planes of the padded batch, then 1/S_b
-    return (size_t)(bpad_of(B) * kt_of(K) * BK * 4 + B * 4 + 256);
+size_t tc_workspace_bytes(int64_t B, int64_t K, int group_size) {
+    // fp16 hi + lo planes of the padded batch, 1/S_b, per-group sums of x' S_b
+    return (size_t)(bpad_of(B) * kt_of(K) * BK * 4 + round256(B * 4) + ngroups_of(K, group_size) * bpad_of(B) * 4 +
+                    256);
 }
 
 cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
-    const TcWorkspace w = carve(workspace, g.B, g.K);
+    const TcWorkspace w = carve(workspace, g.B, g.K, g.group_size);
     const int bn = bn_of(g.B);
     const int64_t bpad = bpad_of(g.B);
+    const int64_t ng = ngroups_of(g.K, g.group_size);
+    const int gsz = ng == 1 ? (int)g.K : g.group_size;
     prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn,
-                                                 g.bits == 4, w.planes, w.inv_s);
+                                                 g.bits == 4, w.planes, w.inv_s, gsz, (int)ng, (int)bpad, w.xsum);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // x' stage counts: 192 KB of planes next to two 16 KB codes stages

@@ -33,17 +33,20 @@ size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
 // batch, shared-memory fit).
 bool gemv_supported(const GemmProblem& p);
 cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
-// int4 codes at batches 1-2 on the integer tensor-core path (mma.sync u4 x s4),
-// when groups are multiples of 64 (or one group), K <= 8192 and the tables
-// can be bulk-copied; launch_gemv routes these problems to it.
+// int4 codes at batches 1-4 on the integer tensor-core path (mma.sync
+// m16n8k32 u8 x s8: codes widened to bytes, x' as three signed base-256
+// digits; batches 3-4 as two launches), when groups are multiples of 64 (or
+// one group), K <= 8192 and the tables can be bulk-copied; launch_gemv routes
+// these problems to it.
 bool gemv_imma_supported(const GemmProblem& p);
 cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
 
 // --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
 // Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
-// single group). Workspace: the fp16 hi/lo planes of x' and 1/S_b.
+// single group). Workspace: the fp16 hi/lo planes of x', 1/S_b and the
+// per-group sums of x' (for zero points that are not integers).
 bool tc_supported(const GemmProblem& p);
-size_t tc_workspace_bytes(int64_t B, int64_t K);
+size_t tc_workspace_bytes(int64_t B, int64_t K, int group_size);
 cudaError_t launch_tc(const GemmProblem& p, void* workspace, cudaStream_t s);
 
 // --- generic tiled SIMT kernel: any shape, reference per-element formula ---
@@ -104,9 +107,8 @@ cudaError_t launch_gptq_block(const double* w, int64_t rows, int64_t ld, const d
 int sm_count();
 
 // Device address (current device) of the library's fault word: kernels OR in
-// 1 when a bounded pipeline mbarrier wait expires, 2 when the tensor-core path
-// meets a zero point that is not an integer in [0, 1023]. nullptr if the
-// symbol cannot be resolved.
+// 1 when a bounded pipeline mbarrier wait expires. nullptr if the symbol
+// cannot be resolved.
 unsigned int* fault_word();
 
 }  // namespace wq

@@ -22,7 +22,12 @@
 //     (different streams, no ordering between them) race on it.
 //   - The first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress while that device is current; make that first call
-//     before capturing a stream.
+//     before capturing a stream. The address is kept per device together with
+//     the CUDA context it belongs to: after a cudaDeviceReset the device has a
+//     new context, and the next call looks the address up again instead of
+//     handing the kernels a pointer into the destroyed one.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "../../include/wq_b200.h"
@@ -37,10 +42,28 @@ constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 // address returned by cudaGetSymbolAddress may be handed to a kernel.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The driver's cuCtxGetCurrent, reached through the runtime (no link-time
+// dependency on libcuda); nullptr if unavailable.
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+    });
+    return fn;
+}
+
 // Device address of g_noalloc_scratch on the current device, looked up once
-// per device (nullptr if the lookup failed).
+// per device and context (nullptr if the lookup failed).
 void* scratch_address(cudaError_t* err) {
     static void* cached[64] = {nullptr};
+    static CUcontext cached_ctx[64] = {nullptr};
     static std::mutex mu;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -48,15 +71,22 @@ void* scratch_address(cudaError_t* err) {
         *err = e != cudaSuccess ? e : cudaErrorInvalidDevice;
         return nullptr;
     }
+    CtxGetCurrentFn get = ctx_get_current();
+    CUcontext ctx = nullptr;
+    if (get != nullptr && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (cached[dev] == nullptr) {
+    if (cached[dev] == nullptr || ctx == nullptr || cached_ctx[dev] != ctx) {
+        // (the lookup makes the device's primary context current if none is;
+        // the context is read again after it)
         void* ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess) {
             *err = e;
             return nullptr;
         }
+        if (get != nullptr && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
         cached[dev] = ptr;
+        cached_ctx[dev] = ctx;
     }
     *err = cudaSuccess;
     return cached[dev];

@@ -23,7 +23,10 @@ every rank. When the whole y is needed on every rank there are two exchanges:
   of once per peer; falls back to peer stores where the switch address is not
   available. Same ordering as p2p.
 * ``exchange="auto"`` (default): nvls, or p2p if symmetric memory cannot be
-  set up on this system.
+  set up on this system. The ranks agree on the choice (a MIN all-reduce of
+  each rank's setup outcome, once after the local allocation and once after
+  the collective rendezvous), so a setup that fails on one rank alone sends
+  every rank to p2p instead of leaving the ranks in different collectives.
 * ``exchange="nccl"``: the kernel writes the local shard, one NCCL all-gather
   collects [world, B, Mp] and a permute kernel lays it out as [B, M].
 """
@@ -76,6 +79,41 @@ def shard_weight(qw: QuantizedWeight, rank: int, world: int) -> QuantizedWeight:
         granularity=qw.granularity,
         channel_scale=qw.channel_scale,
     )
+
+
+def all_ranks_agree(ok: bool, group: dist.ProcessGroup | None, device: torch.device) -> bool:
+    """True on every rank iff ``ok`` is true on every rank (MIN all-reduce)."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(flag.item()) == 1)
+
+
+_SETUP_ERRORS = (RuntimeError, AttributeError, ImportError, ValueError, NotImplementedError)
+
+
+def choose_collectively(setup_local, setup_collective, group: dist.ProcessGroup | None,  # type: ignore[no-untyped-def]
+                        device: torch.device) -> bool:
+    """Run a two-phase setup and agree on its outcome across ranks.
+
+    ``setup_local()`` may fail on any rank alone (an allocation); it returns a
+    state handed to ``setup_collective(state)``, which every rank enters only
+    if every rank's local phase succeeded (it may itself be a collective).
+    Returns True on every rank iff both phases succeeded on every rank; the
+    ranks always take the same collective calls in the same order."""
+    state = None
+    try:
+        state = setup_local()
+        ok = True
+    except _SETUP_ERRORS:
+        ok = False
+    if not all_ranks_agree(ok, group, device):
+        return False
+    try:
+        setup_collective(state)
+        ok = True
+    except _SETUP_ERRORS:
+        ok = False
+    return all_ranks_agree(ok, group, device)
 
 
 def gather_shards(y_local: torch.Tensor, out: torch.Tensor, group: dist.ProcessGroup | None = None) -> None:
@@ -154,25 +192,37 @@ class RowParallelDequantLinear:
             self._peer[batch] = sets
         return self._peer[batch]
 
+    def _nvls_alloc(self, batch: int) -> list[torch.Tensor]:
+        """This rank's two full y buffers in symmetric memory (local; may fail
+        on one rank alone, e.g. out of memory)."""
+        from torch.distributed import _symmetric_memory as symm_mem
+
+        dev = self.shard.codes.device
+        return [symm_mem.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev) for _ in range(2)]
+
+    def _nvls_bind(self, batch: int, fulls: list[torch.Tensor]) -> None:
+        """Collective: binds both buffers across the ranks and records this
+        rank's column pointers in every rank's copy and the NVLink-switch
+        address (0 when the system has none)."""
+        from torch.distributed import _symmetric_memory as symm_mem
+
+        group = self.group if self.group is not None else dist.group.WORLD
+        col = self.rank * self.mp * 4
+        sets = []
+        for full in fulls:
+            handle = symm_mem.rendezvous(full, group)
+            ptrs = [int(p) for p in handle.buffer_ptrs]
+            outs = [ptrs[self.rank] + col] + [ptrs[r] + col for r in range(self.world) if r != self.rank]
+            switch = int(getattr(handle, "multicast_ptr", 0) or 0)
+            sets.append((full, outs, switch + col if switch else 0, handle))
+        self._nvls[batch] = sets
+
     def _nvls_buffers(self, batch: int) -> list[tuple[torch.Tensor, list[int], int, object]]:
         """Two full y buffers in symmetric memory, with this rank's column
         pointers in every rank's copy and the NVLink-switch address (0 when the
         system has none)."""
         if batch not in self._nvls:
-            from torch.distributed import _symmetric_memory as symm_mem
-
-            dev = self.shard.codes.device
-            group = self.group if self.group is not None else dist.group.WORLD
-            col = self.rank * self.mp * 4
-            sets = []
-            for _ in range(2):
-                full = symm_mem.empty((batch, self.world * self.mp), dtype=torch.float32, device=dev)
-                handle = symm_mem.rendezvous(full, group)
-                ptrs = [int(p) for p in handle.buffer_ptrs]
-                outs = [ptrs[self.rank] + col] + [ptrs[r] + col for r in range(self.world) if r != self.rank]
-                switch = int(getattr(handle, "multicast_ptr", 0) or 0)
-                sets.append((full, outs, switch + col if switch else 0, handle))
-            self._nvls[batch] = sets
+            self._nvls_bind(batch, self._nvls_alloc(batch))
         return self._nvls[batch]
 
     def close(self) -> None:
@@ -189,11 +239,11 @@ class RowParallelDequantLinear:
         """y [B, M] on every rank (gather=True), else this rank's [B, Mp] shard."""
         batch = int(x.shape[0])
         if gather and self.world > 1 and self.exchange == "auto":
-            try:
-                self._nvls_buffers(batch)
-                self.exchange = "nvls"
-            except (RuntimeError, AttributeError, ImportError):
-                self.exchange = "p2p"
+            ok = choose_collectively(lambda: self._nvls_alloc(batch), lambda fulls: self._nvls_bind(batch, fulls),
+                                     self.group, self.shard.codes.device)
+            if not ok:
+                self._nvls.pop(batch, None)   # drop a half-built set
+            self.exchange = "nvls" if ok else "p2p"
         if gather and self.world > 1 and self.exchange in ("nvls", "p2p"):
             k = self._calls.get(batch, 0)
             self._calls[batch] = k + 1
