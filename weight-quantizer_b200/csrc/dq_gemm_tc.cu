@@ -52,6 +52,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "fp16_codes.cuh"
 #include "kernels.h"
 
 namespace wq {
@@ -96,6 +97,12 @@ struct Cfg {
     static constexpr int REGS_CTL = 40;
     static constexpr int REGS_DQ = BN >= 128 ? 112 : 88;
     static constexpr int REGS_EPI = BN >= 128 ? 232 : 112;
+    // Batch tiles of 32 (batches 5-32) stack the hi and lo planes into one
+    // MMA of N = 2 BN (the lo rows follow the hi rows in every K tile of the
+    // planes), halving the MMA instructions, which bound this narrow tile;
+    // the accumulator then holds sum A hi and sum A lo side by side.
+    static constexpr bool STACK = BN <= 32;
+    static constexpr int ACCW = STACK ? 2 * BN : BN;      // tensor-memory columns per accumulator
     static_assert(REGS_CTL + DQG * REGS_DQ + REGS_EPI <= (2 + DQG) * LAUNCH_REGS,
                   "register split exceeds the launch's registers");
 };
@@ -178,39 +185,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
-    return d;
-}
-__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
-    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// The integer zero point A is built with: rint(zero) clamped to [0, 1023]
-// (1024 + zi is then exact in fp16; NaN maps to 0 and reaches y through the
-// epilogue's dz term, as it reaches the reference's (code - zero)).
-__device__ __forceinline__ float zero_int(float z) { return fminf(fmaxf(rintf(z), 0.0f), 1023.0f); }
-
-// 8 int4 codes (one 32-bit word, k ascending) -> 8 fp16 values (code - zi)
-// in the order the nibble masks produce them, k0 k4 k1 k5 k2 k6 k3 k7; the
-// prep kernel stores the x' planes of int4 layers in the same order inside
-// every group of 8, so the products pair up without a byte shuffle.
-// zz = half2(1024 + zi) twice.
-__device__ __forceinline__ uint4 dq8_int4(uint32_t w, uint32_t zz) {
-    return make_uint4(hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), zz),          // k0, k4
-                      hsub2_u32(lop3_and_or(w >> 4, 0x000F000Fu, 0x64006400u), zz),     // k1, k5
-                      hsub2_u32(lop3_and_or(w >> 8, 0x000F000Fu, 0x64006400u), zz),     // k2, k6
-                      hsub2_u32(lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u), zz));   // k3, k7
-}
-// 8 int8 codes (two words) -> 8 fp16 (code - zi)
-__device__ __forceinline__ uint4 dq8_int8(uint32_t a, uint32_t b, uint32_t zz) {
-    const uint32_t e = 0x64646464u;
-    return make_uint4(hsub2_u32(__byte_perm(a, e, 0x4140), zz), hsub2_u32(__byte_perm(a, e, 0x4342), zz),
-                      hsub2_u32(__byte_perm(b, e, 0x4140), zz), hsub2_u32(__byte_perm(b, e, 0x4342), zz));
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -231,9 +205,10 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
         : "memory");
 }
 
-// Tensor memory: 512 columns. Columns [0, 2 BN) hold the two group
-// accumulators; the rest is a ring of A stages, each two K tiles wide
-// (2 x 32 columns of packed fp16 pairs, one row per lane).
+// Tensor memory: 512 columns (256 for the narrow tiles, two CTAs per SM).
+// Columns [0, 2 ACCW) hold the two group accumulators; the rest is a ring of
+// A stages, each two K tiles wide (2 x 32 columns of packed fp16 pairs, one
+// row per lane).
 constexpr int kTilesPerA = 2;
 constexpr int kAStageCols = kTilesPerA * BK / 2;
 
@@ -241,7 +216,7 @@ template <int BN, int NS, int BITS>
 struct Smem {
     static constexpr int CB = BITS == 4 ? 32 : 64;        // packed code bytes per row per K tile
     static constexpr int KC = kCodeRowBytes / CB;          // K tiles per codes stage
-    static constexpr int NA = (int)(Cfg<BN>::TMEM_COLS - 2 * BN) / kAStageCols;   // A stages in tensor memory
+    static constexpr int NA = (int)(Cfg<BN>::TMEM_COLS - 2 * Cfg<BN>::ACCW) / kAStageCols;   // A stages in tensor memory
     static constexpr int B_BYTES = BN * 128;               // one plane of one K tile
     static constexpr int STAGE = 2 * B_BYTES;              // hi + lo planes
     static constexpr int C_STAGE = BM * kCodeRowBytes;
@@ -323,7 +298,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::TMEM_SLOT);
-    const uint32_t tmem_a0 = tmem + (uint32_t)(2 * BN);
+    const uint32_t tmem_a0 = tmem + (uint32_t)(2 * C::ACCW);
     bool faulted = false;
     auto wait = [&](uint32_t b, uint32_t parity) {
         if (faulted) return;
@@ -438,7 +413,8 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         if (lane == 0) {
             constexpr int kIssueBatch = 8;
             // kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, N = BN, M = 128
-            const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            constexpr int MMA_N = C::STACK ? 2 * BN : BN;
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(MMA_N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
             const uint64_t b_desc0 = sw128_desc(stage_b(0));
             constexpr uint64_t kPlaneStep = (uint64_t)(L::B_BYTES >> 4);
             int t = 0, sb = 0, sa = 0, h = 0, gin = 0, g = 0;
@@ -462,14 +438,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                     const bool first = gin == 0;
                     const bool last = (gin == p.ktg - 1) || (t == p.KT - 1);
                     const int buf = g & 1;
-                    const uint32_t d = tmem + (uint32_t)(buf * BN);
+                    const uint32_t d = tmem + (uint32_t)(buf * C::ACCW);
                     const uint32_t a_tile = tmem_a0 + (uint32_t)(sa * kAStageCols + h * (BK / 2));
                     const uint64_t b_desc = b_desc0 + (uint64_t)(sb * (L::STAGE >> 4));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t bd = b_desc + 2u * kk;
                         mma_f16_ts(d, a_tile + 8u * kk, bd, idesc, (first && kk == 0) ? 0u : 1u);
-                        mma_f16_ts(d, a_tile + 8u * kk, bd + kPlaneStep, idesc, 1u);
+                        if constexpr (!C::STACK) mma_f16_ts(d, a_tile + 8u * kk, bd + kPlaneStep, idesc, 1u);
                     }
                     mma_commit(empty_b(sb));
                     if (last) {
@@ -618,7 +594,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             const int buf = g & 1, use = g >> 1;
             wait_warp(acc_full(buf), (uint32_t)(use & 1));
             tc_fence_after();
-            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACCW);
             if constexpr (BN > 128) {
                 // 16 columns per load: BN accumulators plus the loaded chunk
                 // stay inside the epilogue's register budget
@@ -630,12 +606,16 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                     for (int i = 0; i < 16; ++i) acc[cc * 16 + i] = fmaf(sc, v[i], acc[cc * 16 + i]);
                 }
             } else {
+                // stacked planes: the hi sums, then the lo sums BN columns further
 #pragma unroll
-                for (int cc = 0; cc < BN / 32; ++cc) {
-                    float v[32];
-                    tmem_ld32(taddr + 32u * cc, v);
+                for (int pl = 0; pl < (C::STACK ? 2 : 1); ++pl) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
+                    for (int cc = 0; cc < BN / 32; ++cc) {
+                        float v[32];
+                        tmem_ld32(taddr + (uint32_t)(pl * BN) + 32u * cc, v);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
+                    }
                 }
             }
             tc_fence_before();
