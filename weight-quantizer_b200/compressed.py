@@ -34,7 +34,7 @@ import torch
 from torch import nn
 
 from . import _kernels
-from .convert import _replace, weight_out_in
+from .convert import _set_module, weight_out_in
 from .linear import QuantizedLinear
 from .quant import QuantizedWeight
 
@@ -333,7 +333,7 @@ def load_compressed(
             raise ValueError(f"model has no module {name!r}") from err
         if not _matches(target, layer):
             raise ValueError(f"module {name!r} does not match the compressed layer's shape")
-        _replace(model, name, layer)
+        _set_module(model, name, layer)
 
     used: set[str] = set()
     for kind in ("param", "buffer"):

@@ -1,30 +1,32 @@
-"""Replace nn.Linear and GPT-2 Conv1D modules with QuantizedLinear on the GPU.
+"""``quantize_model`` on the GPU: replace every nn.Linear / GPT-2 Conv1D by a QuantizedLinear.
 
-Mirror of ptqkit's ``quantize_model`` (src/ptqkit/convert.py:236-293) for the
-RTN, AWQ and GPTQ methods, with the model's parameters on a CUDA device instead of
-the CPU (ptqkit's ``_check_cpu``, convert.py:122-126, becomes a CUDA check):
-every target weight is quantized by the GPU RTN kernel (bit-exact with
-ptqkit's quantize_weight), the GPU AWQ search (``awq.awq_quantize``) or the
-GPU GPTQ sweep (``gptq.gptq_quantize``), and
-the module is replaced by a QuantizedLinear whose ``impl="kernel"`` forward
-runs the dequant-GEMM with the bias added in the kernel's epilogue.
+Same contract as ptqkit's ``quantize_model`` (src/ptqkit/convert.py:236-293):
+RTN needs no data; AWQ and GPTQ calibrate on ``calibration_batches``, either
+in one pass over the model (each target sees the float model's inputs) or
+``sequential=True`` (targets in order, each calibrated with the earlier ones
+already quantized); ``kernel=True`` makes the new layers run the sm_100a
+dequant-GEMM; ``cache_weights`` keeps a dense W_hat on every layer; a model
+that is itself the only target comes back as the replacement layer.
 
-AWQ calibration follows convert.py:26-254: forward pre-hooks collect each
-target's inputs, either as running statistics over one pass of the
-calibration set (channel |x| sums in fp64 and the first 2048 rows,
-ActivationStats) or, with ``sequential=True``, as every input row of one
-target at a time with the earlier targets already replaced. GPTQ takes its
-Hessian X^T X / n from the same capture (an fp64 Gram matrix on the device)
-and runs ``gptq.gptq_quantize``.
+The calibration is built around the device: a ``_Recorder`` context installs
+one forward pre-hook per target and folds every input batch, as it arrives,
+into that target's statistics on the GPU (``_Stats``), keeping only what the
+method needs:
 
-Conv1D stores its weight as [in, out] and computes x @ W; the quantizer stores
-[out, in] for both layouts, so the forward is always x @ W_hat^T + bias
-(convert.py:1-4).
+* AWQ: the per-channel sum of |x| (fp64, this library's fixed-order kernel),
+  the row count, and the first 2048 rows (the search sample, convert.py:26-63);
+* GPTQ: the fp64 Gram matrix X^T X and the row count (Hessian X^T X / n);
+* sequential mode: every input row of the one target being calibrated.
+
+The method itself is one entry of ``_METHODS``: GPU RTN (bit-exact with
+ptqkit's quantize_weight), the GPU AWQ search or the GPU GPTQ sweep.
+Parameters must already live on a CUDA device (ptqkit requires the CPU,
+convert.py:122-126).
 """
 
 from __future__ import annotations
 
-from collections.abc import Sequence
+from collections.abc import Callable, Sequence
 from typing import Any
 
 import torch
@@ -37,202 +39,175 @@ from .linear import QuantizedLinear
 from .quant import Method, QuantConfig, QuantizedWeight, quantize_weight
 
 Batch = torch.Tensor | dict[str, torch.Tensor]
-_SAMPLE_ROWS = 2048
+_SAMPLE_ROWS = 2048   # AWQ search rows (convert.py:26)
 
 
-class ActivationStats:
-    """Running statistics of one target's inputs (convert.py:35-70), on the device:
-    the fp64 Gram matrix X^T X (for GPTQ's Hessian; kept only when asked for),
-    the fp64 sum of |x| per input channel, the row count and the first 2048 rows."""
-
-    def __init__(self, gram: bool = True) -> None:
-        self.keep_gram = gram
-        self.xtx: torch.Tensor | None = None
-        self.abs_sum: torch.Tensor | None = None
-        self.count: int = 0
-        self.sample: torch.Tensor | None = None
-
-    def update(self, hidden: torch.Tensor) -> None:
-        x = hidden.detach().reshape(-1, hidden.shape[-1]).to(dtype=torch.float32)
-        if self.keep_gram:
-            x64 = x.double()
-            gram = x64.transpose(0, 1) @ x64
-            self.xtx = gram if self.xtx is None else self.xtx + gram
-        self.abs_sum = _kernels.channel_abs_sum(x, self.abs_sum)
-        self.count += int(x.shape[0])
-        if self.sample is None:
-            self.sample = x[:_SAMPLE_ROWS].clone()
-        elif int(self.sample.shape[0]) < _SAMPLE_ROWS:
-            need = _SAMPLE_ROWS - int(self.sample.shape[0])
-            self.sample = torch.cat((self.sample, x[:need].clone()), dim=0)
-
-    def hessian(self) -> torch.Tensor:
-        if self.xtx is None or self.count == 0:
-            raise RuntimeError("no calibration rows")
-        return self.xtx / self.count
-
-    def mean_abs(self) -> torch.Tensor:
-        if self.abs_sum is None or self.count == 0:
-            raise RuntimeError("no calibration rows")
-        return (self.abs_sum / self.count).to(dtype=torch.float32)
-
-    def rows(self) -> torch.Tensor:
-        if self.sample is None:
-            raise RuntimeError("no calibration rows")
-        return self.sample
+# ---- targets -------------------------------------------------------------------
 
 
-def _is_conv1d(module: nn.Module) -> bool:
-    return module.__class__.__name__ == "Conv1D" and hasattr(module, "weight")
+def _conv1d(module: nn.Module) -> bool:
+    # GPT-2's Conv1D (transformers) stores its weight as [in, out]
+    return type(module).__name__ == "Conv1D" and hasattr(module, "weight")
 
 
 def iter_targets(model: nn.Module) -> list[tuple[str, nn.Module]]:
-    """Every nn.Linear / Conv1D with a 2-D weight, in named_modules order
-    (convert.py:73-82); modules that are already QuantizedLinear are skipped."""
-    found: list[tuple[str, nn.Module]] = []
-    for name, module in model.named_modules():
-        if isinstance(module, QuantizedLinear):
-            continue
-        if isinstance(module, nn.Linear) or _is_conv1d(module):
-            weight = getattr(module, "weight", None)
-            if isinstance(weight, torch.Tensor) and weight.ndim == 2:
-                found.append((name, module))
-    return found
+    """(name, module) of every nn.Linear / Conv1D with a 2-D weight, in
+    named_modules order; layers that are already quantized are left out."""
+    return [
+        (name, m) for name, m in model.named_modules()
+        if not isinstance(m, QuantizedLinear)
+        and (isinstance(m, nn.Linear) or _conv1d(m))
+        and isinstance(getattr(m, "weight", None), torch.Tensor) and m.weight.ndim == 2
+    ]
 
 
 def weight_out_in(module: nn.Module) -> torch.Tensor:
-    """The module's weight as [out, in] (convert.py:85-93)."""
-    weight = getattr(module, "weight", None)
-    if not isinstance(weight, torch.Tensor) or weight.ndim != 2:
-        raise TypeError(f"unsupported module {module.__class__.__name__}")
-    if isinstance(module, nn.Linear):
-        return weight.detach()
-    if _is_conv1d(module):
-        return weight.detach().transpose(0, 1).contiguous()
-    raise TypeError(f"unsupported module {module.__class__.__name__}")
+    """The module's weight as [out, in] (Conv1D's [in, out] transposed)."""
+    w = getattr(module, "weight", None)
+    if isinstance(w, torch.Tensor) and w.ndim == 2:
+        if isinstance(module, nn.Linear):
+            return w.detach()
+        if _conv1d(module):
+            return w.detach().t().contiguous()
+    raise TypeError(f"unsupported module {type(module).__name__}")
 
 
-def _bias_of(module: nn.Module) -> torch.Tensor | None:
+def _set_module(root: nn.Module, name: str, new: nn.Module) -> None:
+    parent_name, _, leaf = name.rpartition(".")
+    setattr(root.get_submodule(parent_name) if parent_name else root, leaf, new)
+
+
+# ---- calibration ----------------------------------------------------------------
+
+
+class _Stats:
+    """What one target's inputs contribute to its method, kept on the GPU."""
+
+    def __init__(self, *, gram: bool, abs_sum: bool, sample: bool, all_rows: bool) -> None:
+        self.want_gram, self.want_abs, self.want_sample, self.want_all = gram, abs_sum, sample, all_rows
+        self.n = 0
+        self.gram: torch.Tensor | None = None
+        self.abs: torch.Tensor | None = None
+        self.sample: list[torch.Tensor] = []
+        self.n_sample = 0
+        self.rows: list[torch.Tensor] = []
+
+    def add(self, x: torch.Tensor) -> None:
+        x = x.detach().reshape(-1, x.shape[-1]).to(dtype=torch.float32)
+        self.n += int(x.shape[0])
+        if self.want_gram:
+            x64 = x.double()
+            g = x64.t() @ x64
+            self.gram = g if self.gram is None else self.gram + g
+        if self.want_abs:
+            self.abs = _kernels.channel_abs_sum(x, self.abs)
+        if self.want_sample and self.n_sample < _SAMPLE_ROWS:
+            take = x[: _SAMPLE_ROWS - self.n_sample].clone()
+            self.sample.append(take)
+            self.n_sample += int(take.shape[0])
+        if self.want_all:
+            self.rows.append(x.clone())
+
+    def _need_rows(self) -> None:
+        if self.n == 0:
+            raise RuntimeError("no calibration rows")
+
+    def hessian(self) -> torch.Tensor:
+        self._need_rows()
+        if self.want_all:
+            r = torch.cat(self.rows).double()
+            return r.t() @ r / float(r.shape[0])
+        assert self.gram is not None
+        return self.gram / self.n
+
+    def awq_inputs(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """(search rows, mean |x| per channel)."""
+        self._need_rows()
+        if self.want_all:
+            r = torch.cat(self.rows)
+            return r[:_SAMPLE_ROWS], channel_mean_abs(r)
+        assert self.abs is not None
+        return torch.cat(self.sample), (self.abs / self.n).to(dtype=torch.float32)
+
+
+class _Recorder:
+    """Context manager: forward pre-hooks feeding each target's ``_Stats``."""
+
+    def __init__(self, targets: Sequence[tuple[str, nn.Module]], make: Callable[[], _Stats]) -> None:
+        self.targets = list(targets)
+        self.stats = {name: make() for name, _ in self.targets}
+        self._handles: list[Any] = []
+
+    def __enter__(self) -> _Recorder:
+        for name, module in self.targets:
+            def hook(_: nn.Module, args: tuple[Any, ...], *, name: str = name) -> None:
+                if not args or not isinstance(args[0], torch.Tensor):
+                    raise TypeError(f"{name} did not receive a tensor input")
+                self.stats[name].add(args[0])
+            self._handles.append(module.register_forward_pre_hook(hook))
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        for h in self._handles:
+            h.remove()
+        self._handles.clear()
+
+
+def _run(model: nn.Module, batches: Sequence[Batch]) -> None:
+    for batch in batches:
+        if isinstance(batch, dict):
+            model(**batch)
+        else:
+            model(batch)
+
+
+def _record(model: nn.Module, targets: Sequence[tuple[str, nn.Module]], batches: Sequence[Batch],
+            method: Method, all_rows: bool) -> dict[str, _Stats]:
+    def make() -> _Stats:
+        if all_rows:
+            return _Stats(gram=False, abs_sum=False, sample=False, all_rows=True)
+        return _Stats(gram=method is Method.GPTQ, abs_sum=method is Method.AWQ, sample=method is Method.AWQ,
+                      all_rows=False)
+
+    with _Recorder(targets, make) as rec:
+        _run(model, batches)
+    return rec.stats
+
+
+# ---- methods ----------------------------------------------------------------------
+
+
+def _rtn(w: torch.Tensor, cfg: QuantConfig, st: _Stats | None) -> tuple[QuantizedWeight, float | None]:
+    return quantize_weight(w, cfg), None
+
+
+def _awq(w: torch.Tensor, cfg: QuantConfig, st: _Stats | None) -> tuple[QuantizedWeight, float | None]:
+    if st is None:
+        raise ValueError("AWQ requires calibration activations")
+    rows, mean_abs = st.awq_inputs()
+    return awq_quantize(w, rows, cfg, mean_abs=mean_abs)
+
+
+def _gptq(w: torch.Tensor, cfg: QuantConfig, st: _Stats | None) -> tuple[QuantizedWeight, float | None]:
+    if st is None:
+        raise ValueError("GPTQ requires calibration activations")
+    return gptq_quantize(w, st.hessian(), cfg), None
+
+
+_METHODS: dict[Method, Callable[[torch.Tensor, QuantConfig, _Stats | None], tuple[QuantizedWeight, float | None]]] = {
+    Method.RTN: _rtn, Method.AWQ: _awq, Method.GPTQ: _gptq,
+}
+
+
+def _layer(module: nn.Module, cfg: QuantConfig, st: _Stats | None, impl: str) -> QuantizedLinear:
+    qw, alpha = _METHODS[cfg.method](weight_out_in(module), cfg, st)
     bias = getattr(module, "bias", None)
-    if not isinstance(bias, torch.Tensor):
-        return None
-    return bias.detach()
-
-
-def _replace(root: nn.Module, name: str, new: nn.Module) -> None:
-    parent: nn.Module = root
-    parts = name.split(".")
-    for part in parts[:-1]:
-        child = getattr(parent, part)
-        if not isinstance(child, nn.Module):
-            raise TypeError(f"{part} is not a module")
-        parent = child
-    setattr(parent, parts[-1], new)
-
-
-def _check_cuda(model: nn.Module) -> None:
-    for param in model.parameters():
-        if param.device.type != "cuda":
-            raise RuntimeError("quantize_model expects CUDA parameters")
-
-
-def _prepare(model: nn.Module) -> None:
-    model.eval()
-    config = getattr(model, "config", None)
-    if config is not None and getattr(config, "use_cache", None) is not None:
-        config.use_cache = False
-
-
-def _forward(model: nn.Module, batch: Batch) -> None:
-    if isinstance(batch, dict):
-        model(**batch)
-    else:
-        model(batch)
-
-
-def _as_batches(batches: Sequence[Batch]) -> list[Batch]:
-    if len(batches) == 0:
-        raise ValueError("calibration_batches is empty")
-    return list(batches)
-
-
-def _capture_all(model: nn.Module, names: list[tuple[str, nn.Module]],
-                 batches: Sequence[Batch], gram: bool = True) -> dict[str, ActivationStats]:
-    """One pass of the calibration set with a statistics hook on every target (convert.py:140-162)."""
-    stats = {name: ActivationStats(gram) for name, _ in names}
-    handles = []
-    for name, module in names:
-
-        def hook(mod: nn.Module, args: tuple[Any, ...], *, name: str = name) -> None:
-            del mod
-            if not args or not isinstance(args[0], torch.Tensor):
-                raise TypeError(f"{name} did not receive a tensor input")
-            stats[name].update(args[0])
-
-        handles.append(module.register_forward_pre_hook(hook))
-    try:
-        for batch in batches:
-            _forward(model, batch)
-    finally:
-        for handle in handles:
-            handle.remove()
-    return stats
-
-
-def _capture_one(model: nn.Module, name: str, module: nn.Module, batches: Sequence[Batch]) -> torch.Tensor:
-    """Every input row of one target over the calibration set (convert.py:165-189)."""
-    chunks: list[torch.Tensor] = []
-
-    def hook(mod: nn.Module, args: tuple[Any, ...]) -> None:
-        del mod
-        if not args or not isinstance(args[0], torch.Tensor):
-            raise TypeError(f"{name} did not receive a tensor input")
-        chunks.append(args[0].detach().reshape(-1, args[0].shape[-1]).to(dtype=torch.float32))
-
-    handle = module.register_forward_pre_hook(hook)
-    try:
-        for batch in batches:
-            _forward(model, batch)
-    finally:
-        handle.remove()
-    if not chunks:
-        raise RuntimeError(f"no activations captured for {name}")
-    return torch.cat(chunks, dim=0)
-
-
-def _module_from(qw: QuantizedWeight, source: nn.Module, *, kernel: bool, alpha: float | None) -> QuantizedLinear:
-    layer = QuantizedLinear(qw, _bias_of(source), impl="kernel" if kernel else "reference")
+    layer = QuantizedLinear(qw, bias.detach() if isinstance(bias, torch.Tensor) else None, impl=impl)
     layer.awq_alpha = alpha
     return layer
 
 
-def _quantize_one(weight: torch.Tensor, config: QuantConfig, stats: ActivationStats | None,
-                  rows: torch.Tensor | None) -> tuple[QuantizedWeight, float | None]:
-    """RTN, or AWQ from captured statistics or rows (convert.py:206-233)."""
-    if config.method is Method.RTN:
-        return quantize_weight(weight, config), None
-    if config.method is Method.GPTQ:
-        if stats is None and rows is None:
-            raise ValueError("GPTQ requires calibration activations")
-        if rows is not None and stats is None:
-            r64 = rows.double()
-            hessian = r64.transpose(0, 1) @ r64 / float(rows.shape[0])
-        else:
-            assert stats is not None
-            hessian = stats.hessian()
-        return gptq_quantize(weight, hessian, config), None
-    if config.method is Method.AWQ:
-        if rows is None and stats is None:
-            raise ValueError("AWQ requires calibration activations")
-        if stats is not None and rows is None:
-            sample = stats.rows()
-            mean_abs = stats.mean_abs()
-        else:
-            assert rows is not None
-            sample = rows[:_SAMPLE_ROWS]
-            mean_abs = channel_mean_abs(rows)
-        return awq_quantize(weight, sample, config, mean_abs=mean_abs)
-    raise ValueError(f"unknown method {config.method}")
+# ---- the model pass -----------------------------------------------------------------
 
 
 def quantize_model(
@@ -244,55 +219,45 @@ def quantize_model(
     kernel: bool = False,
     cache_weights: bool = False,
 ) -> nn.Module:
-    """Quantize every Linear and Conv1D in ``model`` in place (convert.py:236-293).
-
-    ``kernel=True`` makes the layers run the sm_100a dequant-GEMM; otherwise
-    they use ptqkit's reference dense reconstruction. ``cache_weights`` keeps a
-    dense W_hat on every layer (a plain fp32 GEMM forward). Returns the model,
-    or the replacement layer when the model itself is the only target.
-    """
-    _check_cuda(model)
-    _prepare(model)
-    targets = iter_targets(model)
-    if config.method is not Method.RTN and calibration_batches is None:
+    """Quantize every Linear and Conv1D of ``model`` in place on the GPU (see the module docstring)."""
+    if any(p.device.type != "cuda" for p in model.parameters()):
+        raise RuntimeError("quantize_model expects CUDA parameters")
+    model.eval()
+    hf_config = getattr(model, "config", None)
+    if hf_config is not None and getattr(hf_config, "use_cache", None) is not None:
+        hf_config.use_cache = False
+    calibrated = config.method is not Method.RTN
+    if calibrated and calibration_batches is None:
         raise ValueError(f"{config.method.value} requires calibration_batches")
-    batches = [] if calibration_batches is None else _as_batches(calibration_batches)
+    batches = [] if calibration_batches is None else list(calibration_batches)
+    if calibration_batches is not None and not batches:
+        raise ValueError("calibration_batches is empty")
+    impl = "kernel" if kernel else "reference"
+    targets = iter_targets(model)
+    root_only = len(targets) == 1 and targets[0][0] == ""
 
+    done: list[QuantizedLinear] = []
     with torch.inference_mode():
-        if len(targets) == 1 and targets[0][0] == "":
-            module = targets[0][1]
-            stats = None
-            rows = None
-            if config.method is not Method.RTN:
-                if sequential:
-                    rows = _capture_one(model, "root", module, batches)
-                else:
-                    stats = _capture_all(model, [("root", module)], batches, config.method is Method.GPTQ)["root"]
-            qw, alpha = _quantize_one(weight_out_in(module), config, stats, rows)
-            layer = _module_from(qw, module, kernel=kernel, alpha=alpha)
+        if calibrated and sequential:
+            # one target at a time; the quantized layers before it keep a dense
+            # W_hat so that later passes run a plain GEMM through them
+            for name, module in targets:
+                st = _record(model, [(name, module)], batches, config.method, all_rows=True)[name]
+                layer = _layer(module, config, st, impl)
+                layer.materialize()
+                done.append(layer)
+                if not root_only:
+                    _set_module(model, name, layer)
+        else:
+            stats = _record(model, targets, batches, config.method, all_rows=False) if calibrated else {}
+            for name, module in targets:
+                layer = _layer(module, config, stats.get(name), impl)
+                done.append(layer)
+                if not root_only:
+                    _set_module(model, name, layer)
+        for layer in (done if root_only else [m for m in model.modules() if isinstance(m, QuantizedLinear)]):
             if cache_weights:
                 layer.materialize()
-            return layer
-        if config.method is Method.RTN or not sequential:
-            stats_map: dict[str, ActivationStats] | None = None
-            if config.method is not Method.RTN:
-                stats_map = _capture_all(model, targets, batches, config.method is Method.GPTQ)
-            for name, module in targets:
-                stats = None if stats_map is None else stats_map[name]
-                qw, alpha = _quantize_one(weight_out_in(module), config, stats, None)
-                _replace(model, name, _module_from(qw, module, kernel=kernel, alpha=alpha))
-        else:
-            for name, module in targets:
-                rows = _capture_one(model, name, module, batches)
-                qw, alpha = _quantize_one(weight_out_in(module), config, None, rows)
-                layer = _module_from(qw, module, kernel=kernel, alpha=alpha)
-                # a cached reconstruction keeps later calibration passes on the fp32 GEMM
-                layer.materialize()
-                _replace(model, name, layer)
-        for module in model.modules():
-            if isinstance(module, QuantizedLinear):
-                if cache_weights:
-                    module.materialize()
-                else:
-                    module.clear_cache()
-    return model
+            else:
+                layer.clear_cache()
+    return done[0] if root_only else model

@@ -172,11 +172,10 @@ int wq_selftest_expired_wait(uint32_t max_polls, void* stream) {
 }
 
 size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
-    (void)M;
     if (B <= 0 || K <= 0 || group_size <= 0 || (bits != 4 && bits != 8)) return 0;
     if (B <= wq::kGemvMaxBatch) return wq::gemv_workspace_bytes(B, K, bits);
     const bool single_group = group_size >= K;
-    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, K, group_size);
+    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, M, K, group_size, bits);
     return 0;
 }
 
@@ -260,7 +259,7 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
         fan_out();
         e = wq::launch_gemv(p, workspace, s);
     } else if (wq::tc_supported(p)) {
-        const size_t need = wq::tc_workspace_bytes(B, K, group_size);
+        const size_t need = wq::tc_workspace_bytes(B, M, K, group_size, bits);
         if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
         if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
         fan_out();

@@ -121,6 +121,9 @@ struct TcParams {
     int n_extra;
     float* y_all;         // NVLink-switch address reaching every rank's y, or nullptr
     const float* bias;    // [M] or nullptr
+    float* part;          // split-K partial tiles [splits][tiles_m * tiles_n][BN][BM]
+    int* counters;        // split-K arrivals per output tile (zeroed by the prep kernel)
+    int splits, gran;     // K splits (grid.y) and the K tiles a split boundary is a multiple of
     unsigned int* fault;
     int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
@@ -227,6 +230,7 @@ struct Smem {
     static constexpr int NBAR = 2 * NS + 2 * NA + 2 * kNC + 4;
     static constexpr int TMEM_SLOT = BAR_OFF + 8 * NBAR;
     static constexpr int READY = TMEM_SLOT + 8;   // u32: tiles whose operands are ready
+    static constexpr int FLAG = TMEM_SLOT + 12;   // u32: this CTA adds the split-K partials
     static constexpr int TOTAL = TMEM_SLOT + 16;
     static_assert(STAGE % 1024 == 0 && C_STAGE % 1024 == 0, "tiles must stay 1024-byte aligned for the 128-byte swizzle");
     static_assert(TOTAL + 1024 <= 227 * 1024, "stage rings exceed the shared memory of one CTA");
@@ -234,7 +238,7 @@ struct Smem {
     static_assert(KC % kTilesPerA == 0, "a codes stage must hold whole A stages");
 };
 
-template <int BN, int NS, int BITS>
+template <int BN, int NS, int BITS, bool SPLIT>
 __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     dq_gemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap map_q) {
     using L = Smem<BN, NS, BITS>;
@@ -266,7 +270,23 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     const int m_tile = inner / bw;
     const int n_tile = band * kBand + (inner - m_tile * bw);
     const int m0 = m_tile * BM, n0 = n_tile * BN;
-    const int n_astages = (p.KT + kTilesPerA - 1) / kTilesPerA;
+    // split-K: this CTA's K tiles [t0, t0 + KTL) and groups [g0, g0 + NGL);
+    // split boundaries fall on group and code-box boundaries (p.gran tiles)
+    // (the unsplit instantiation reads the kernel parameters as they are)
+    int s_t0 = 0, s_ktl = 0, s_g0 = 0, s_ngl = 0;
+    if constexpr (SPLIT) {
+        const int nu = (p.KT + p.gran - 1) / p.gran;
+        const int su0 = (int)blockIdx.y * nu / p.splits, su1 = ((int)blockIdx.y + 1) * nu / p.splits;
+        s_t0 = su0 * p.gran;
+        s_ktl = min(su1 * p.gran, p.KT) - s_t0;
+        s_g0 = s_t0 / p.ktg;
+        s_ngl = (s_ktl + p.ktg - 1) / p.ktg;
+    }
+    auto T0 = [&]() -> int { if constexpr (SPLIT) return s_t0; else return 0; };
+    auto KTL = [&]() -> int { if constexpr (SPLIT) return s_ktl; else return p.KT; };
+    auto G0 = [&]() -> int { if constexpr (SPLIT) return s_g0; else return 0; };
+    auto NGL = [&]() -> int { if constexpr (SPLIT) return s_ngl; else return p.ngroups; };
+    const int n_astages = (KTL() + kTilesPerA - 1) / kTilesPerA;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -335,10 +355,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         // x' planes: one bulk copy of both planes of a K tile per stage
         if (lane == 0) {
             const uint32_t tile_bytes = (uint32_t)L::STAGE;
-            const unsigned char* src = p.planes + (size_t)n_tile * p.KT * tile_bytes;
+            const unsigned char* src = p.planes + ((size_t)n_tile * p.KT + T0()) * tile_bytes;
             int s = 0;
             uint32_t ph = 0;
-            for (int t = 0; t < p.KT; ++t) {
+            for (int t = 0; t < KTL(); ++t) {
                 if (t >= NS) wait(empty_b(s), ph ^ 1u);
                 mbar_arrive_expect_tx(full_b(s), tile_bytes);
                 bulk_copy_g2s(stage_b(s), src, tile_bytes, full_b(s));
@@ -348,19 +368,19 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                     ph ^= 1u;
                 }
             }
-            drain(NS, p.KT, full_b);
+            drain(NS, KTL(), full_b);
         }
       } else if (warp == kWarpCodes) {
         // packed codes: KC K tiles per 2D box (128 rows x 128 bytes, 128-byte
         // swizzle so that the dequant threads read them without bank conflicts)
         if (lane == 0) {
-            const int nct = (p.KT + L::KC - 1) / L::KC;
+            const int nct = (KTL() + L::KC - 1) / L::KC;
             int c = 0;
             uint32_t ph = 0;
             for (int ct = 0; ct < nct; ++ct) {
                 if (ct >= kNC) wait(c_empty(c), ph ^ 1u);
                 mbar_arrive_expect_tx(c_full(c), (uint32_t)L::C_STAGE);
-                tma_load_2d(stage_c(c), &map_q, ct * kCodeRowBytes, m0, c_full(c));
+                tma_load_2d(stage_c(c), &map_q, (T0() / L::KC + ct) * kCodeRowBytes, m0, c_full(c));
                 if (++c == kNC) {
                     c = 0;
                     ph ^= 1u;
@@ -378,14 +398,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         if (lane == 0) {
             int sb = 0, sa = 0, h = 0, gin = 0, g = 0;
             uint32_t phb = 0, pha = 0;
-            for (int t = 0; t < p.KT; ++t) {
+            for (int t = 0; t < KTL(); ++t) {
                 const int use = g >> 1;
                 if (gin == 0 && use > 0) wait(acc_empty(g & 1), (uint32_t)((use - 1) & 1));
                 wait(full_b(sb), phb);
                 if (h == 0) wait(full_a(sa), pha);
                 asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(sbase + L::READY), "r"((uint32_t)(t + 1))
                              : "memory");
-                if ((gin == p.ktg - 1) || (t == p.KT - 1)) {
+                if ((gin == p.ktg - 1) || (t == KTL() - 1)) {
                     gin = 0;
                     ++g;
                 } else {
@@ -418,7 +438,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             const uint64_t b_desc0 = sw128_desc(stage_b(0));
             constexpr uint64_t kPlaneStep = (uint64_t)(L::B_BYTES >> 4);
             int t = 0, sb = 0, sa = 0, h = 0, gin = 0, g = 0;
-            while (t < p.KT) {
+            while (t < KTL()) {
                 uint32_t ready = 0;
                 uint32_t polls = 0;
                 for (;;) {
@@ -436,7 +456,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                 tc_fence_after();
                 for (int i = 0; i < n; ++i, ++t) {
                     const bool first = gin == 0;
-                    const bool last = (gin == p.ktg - 1) || (t == p.KT - 1);
+                    const bool last = (gin == p.ktg - 1) || (t == KTL() - 1);
                     const int buf = g & 1;
                     const uint32_t d = tmem + (uint32_t)(buf * C::ACCW);
                     const uint32_t a_tile = tmem_a0 + (uint32_t)(sa * kAStageCols + h * (BK / 2));
@@ -455,7 +475,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                     } else {
                         ++gin;
                     }
-                    if (h == kTilesPerA - 1 || t == p.KT - 1) mma_commit(empty_a(sa));
+                    if (h == kTilesPerA - 1 || t == KTL() - 1) mma_commit(empty_a(sa));
                     if (++sb == NS) sb = 0;
                     if (++h == kTilesPerA) {
                         h = 0;
@@ -463,7 +483,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                     }
                 }
             }
-            drain(NS, p.KT, empty_b);
+            drain(NS, KTL(), empty_b);
             drain(NA, n_astages, empty_a);
         }
       }
@@ -484,12 +504,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         // Zero points of groups g + 1 .. g + 4 are in flight while group g is
         // processed: every thread reads its own row, so these loads are not
         // coalesced and take longer than a few K tiles under load.
-        const float* zrow = p.zeros + srow * p.groups;
+        const float* zrow = p.zeros + srow * p.groups + G0();
         float z_cur = __ldg(zrow);
-        float z_n1 = p.ngroups > 1 ? __ldg(zrow + 1) : 0.0f;
-        float z_n2 = p.ngroups > 2 ? __ldg(zrow + 2) : 0.0f;
-        float z_n3 = p.ngroups > 3 ? __ldg(zrow + 3) : 0.0f;
-        float z_n4 = p.ngroups > 4 ? __ldg(zrow + 4) : 0.0f;
+        float z_n1 = NGL() > 1 ? __ldg(zrow + 1) : 0.0f;
+        float z_n2 = NGL() > 2 ? __ldg(zrow + 2) : 0.0f;
+        float z_n3 = NGL() > 3 ? __ldg(zrow + 3) : 0.0f;
+        float z_n4 = NGL() > 4 ? __ldg(zrow + 4) : 0.0f;
         int g = 0, gin = h_begin;   // this warp's next tile t = 2 ja + h is tile gin of group g
         auto next_group = [&]() {
             gin -= p.ktg;
@@ -498,10 +518,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             z_n1 = z_n2;
             z_n2 = z_n3;
             z_n3 = z_n4;
-            if (g + 4 < p.ngroups) z_n4 = __ldg(zrow + g + 4);
+            if (g + 4 < NGL()) z_n4 = __ldg(zrow + g + 4);
         };
         while (gin >= p.ktg) next_group();
-        const int nct = (p.KT + L::KC - 1) / L::KC;
+        const int nct = (KTL() + L::KC - 1) / L::KC;
         int sa = 0, c = 0, ja = 0;
         uint32_t pha = 0, cph = 0;
         for (int ct = 0; ct < nct; ++ct) {
@@ -512,7 +532,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                 tc_fence_after();
                 for (int h = h_begin; h < h_end; ++h) {
                   const int t = kTilesPerA * ja + h;
-                  if (t < p.KT) {
+                  if (t < KTL()) {
                     const int kin = kTilesPerA * js + h;   // K tile inside the codes stage
                     const __half zh = __float2half_rn(1024.0f + zero_int(z_cur));   // exact
                     const uint32_t zz = (uint32_t)__half_as_ushort(zh) * 0x10001u;
@@ -579,18 +599,18 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
 #pragma unroll
         for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
         // scales of groups g + 1 .. g + 4 are in flight while group g is read
-        const float* srow_p = p.scales + srow * p.groups;
-        float sc_n1 = p.ngroups > 1 ? __ldg(srow_p + 1) : 0.0f;
-        float sc_n2 = p.ngroups > 2 ? __ldg(srow_p + 2) : 0.0f;
-        float sc_n3 = p.ngroups > 3 ? __ldg(srow_p + 3) : 0.0f;
-        float sc_n4 = p.ngroups > 4 ? __ldg(srow_p + 4) : 0.0f;
+        const float* srow_p = p.scales + srow * p.groups + G0();
+        float sc_n1 = NGL() > 1 ? __ldg(srow_p + 1) : 0.0f;
+        float sc_n2 = NGL() > 2 ? __ldg(srow_p + 2) : 0.0f;
+        float sc_n3 = NGL() > 3 ? __ldg(srow_p + 3) : 0.0f;
+        float sc_n4 = NGL() > 4 ? __ldg(srow_p + 4) : 0.0f;
         float sc = __ldg(srow_p);
         // zero points of groups g + 1, g + 2 in flight, for the dz term
-        const float* zrow_p = p.zeros + srow * p.groups;
+        const float* zrow_p = p.zeros + srow * p.groups + G0();
         float zc = __ldg(zrow_p);
-        float z_n1 = p.ngroups > 1 ? __ldg(zrow_p + 1) : 0.0f;
-        float z_n2 = p.ngroups > 2 ? __ldg(zrow_p + 2) : 0.0f;
-        for (int g = 0; g < p.ngroups; ++g) {
+        float z_n1 = NGL() > 1 ? __ldg(zrow_p + 1) : 0.0f;
+        float z_n2 = NGL() > 2 ? __ldg(zrow_p + 2) : 0.0f;
+        for (int g = 0; g < NGL(); ++g) {
             const int buf = g & 1, use = g >> 1;
             wait_warp(acc_full(buf), (uint32_t)(use & 1));
             tc_fence_after();
@@ -626,7 +646,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             const float dz = zc - zero_int(zc);
             if (__any_sync(0xffffffffu, dz != 0.0f)) {
                 const float cz = -(sc * dz);
-                const float4* xs = reinterpret_cast<const float4*>(p.xsum + (int64_t)g * p.bpad + n0);
+                const float4* xs = reinterpret_cast<const float4*>(p.xsum + (int64_t)(G0() + g) * p.bpad + n0);
 #pragma unroll
                 for (int i = 0; i < BN / 4; ++i) {
                     const float4 v = __ldg(xs + i);
@@ -638,14 +658,46 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             }
             zc = z_n1;
             z_n1 = z_n2;
-            if (g + 3 < p.ngroups) z_n2 = __ldg(zrow_p + g + 3);
+            if (g + 3 < NGL()) z_n2 = __ldg(zrow_p + g + 3);
             sc = sc_n1;
             sc_n1 = sc_n2;
             sc_n2 = sc_n3;
             sc_n3 = sc_n4;
-            if (g + 5 < p.ngroups) sc_n4 = __ldg(srow_p + g + 5);
+            if (g + 5 < NGL()) sc_n4 = __ldg(srow_p + g + 5);
         }
-        if (m < p.M) {
+        bool write = true;
+        if constexpr (SPLIT) {
+            // Split-K: the CTA's sums go to its partial slot; the last of the
+            // tile's splits to arrive adds all slots in split order (a fixed
+            // order, whichever CTA is last) and writes y.
+            const int tile = m_tile * p.tiles_n + n_tile;
+            const size_t tile_stride = (size_t)p.tiles_m * p.tiles_n * BN * BM;
+            float* mine = p.part + (size_t)blockIdx.y * tile_stride + (size_t)tile * BN * BM;
+#pragma unroll
+            for (int i = 0; i < BN; ++i) mine[i * BM + r] = acc[i];
+            __threadfence();
+            named_barrier(1, 128);   // the epilogue warpgroup
+            volatile uint32_t* flag = reinterpret_cast<volatile uint32_t*>(smem + L::FLAG);
+            if (warp == kWarpEpi0 && lane == 0) {
+                const int prev = atomicAdd(p.counters + tile, 1);
+                const bool last = prev == p.splits - 1;
+                if (last) p.counters[tile] = 0;
+                *flag = last ? 1u : 0u;
+            }
+            named_barrier(1, 128);
+            write = *flag != 0u;
+            if (write) {
+                __threadfence();
+#pragma unroll
+                for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+                for (int sp = 0; sp < p.splits; ++sp) {
+                    const float* src = p.part + (size_t)sp * tile_stride + (size_t)tile * BN * BM;
+#pragma unroll
+                    for (int i = 0; i < BN; ++i) acc[i] += __ldcg(src + i * BM + r);
+                }
+            }
+        }
+        if (write && m < p.M) {
             // y = acc * 2^-S_b, then the layer's bias (linear.py:99-100) as one
             // fp32 add after the product, like the reference (the _rn intrinsics
             // keep the two roundings apart). Without a bias the add is of -0.0,
@@ -695,9 +747,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
 // sums groups w, w + 8, ..., lanes strided then a butterfly: a fixed order).
 __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float* channel, int B, int K, int KT,
                                                      int BN, bool nibble_order, unsigned char* planes, float* inv_s,
-                                                     int gsz, int ngroups, int bpad, float* xsum) {
+                                                     int gsz, int ngroups, int bpad, float* xsum, int* counters,
+                                                     int ncounters) {
     __shared__ float red[8];
     const int b = blockIdx.x;
+    if (b == 0)   // split-K arrival counters of the tensor-core kernel that follows
+        for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
     const bool real = b < B;
     const float* xb = x + (int64_t)(real ? b : 0) * K;
     float mx = 0.0f;
@@ -807,27 +862,69 @@ int64_t bpad_of(int64_t B) { const int bn = bn_of(B); return (B + bn - 1) / bn *
 int64_t ngroups_of(int64_t K, int group_size) { return group_size >= K ? 1 : (K + group_size - 1) / group_size; }
 int64_t round256(int64_t v) { return (v + 255) / 256 * 256; }
 
+// Split-K plan. When the output tiles fill less than half of the SMs' CTA
+// slots (small layers, or few rows per GPU), each tile's K range is cut into
+// `splits` parts on boundaries of `gran` K tiles: a multiple of the group (so
+// every part holds whole groups) and of the code stage (so every part starts
+// a TMA box). Layers of one group are not split.
+struct SplitPlan {
+    int splits, gran;
+};
+
+SplitPlan split_plan(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
+    SplitPlan sp{1, 1};
+    const int64_t KT = kt_of(K);
+    if (ngroups_of(K, group_size) < 2) return sp;
+    const int bn = bn_of(B);
+    const int64_t tiles = ((M + BM - 1) / BM) * ((B + bn - 1) / bn);
+    const int64_t slots = (int64_t)sm_count() * (bn >= 128 ? 1 : 2);
+    if (2 * tiles > slots) return sp;
+    const int kc = kCodeRowBytes / (bits == 4 ? 32 : 64);   // K tiles per code stage
+    const int ktg = group_size / BK;
+    int g = ktg;
+    while (g % kc != 0) g += ktg;                            // lcm(ktg, kc)
+    const int64_t units = (KT + g - 1) / g;
+    int64_t n = slots / tiles;
+    if (n > units) n = units;
+    if (n > 16) n = 16;
+    sp.splits = (int)(n < 1 ? 1 : n);
+    sp.gran = g;
+    return sp;
+}
+
 // Workspace: [planes: bpad * KT * BK * 4 B][inv_s: B floats, padded to 256 B]
-// [xsum: ngroups * bpad floats]
+// [xsum: ngroups * bpad floats][split-K partial tiles][split-K counters]
 struct TcWorkspace {
     unsigned char* planes;
     float* inv_s;
     float* xsum;
+    float* part;
+    int* counters;
+    SplitPlan plan;
+    int64_t tiles;
 };
 
-TcWorkspace carve(void* ws, int64_t B, int64_t K, int group_size) {
+TcWorkspace carve(void* ws, int64_t B, int64_t M, int64_t K, int group_size, int bits) {
     unsigned char* p = static_cast<unsigned char*>(ws);
     TcWorkspace w;
+    const int bn = bn_of(B);
+    w.plan = split_plan(B, M, K, group_size, bits);
+    w.tiles = ((M + BM - 1) / BM) * ((B + bn - 1) / bn);
     const int64_t planes = bpad_of(B) * kt_of(K) * BK * 4;
     w.planes = p;
-    w.inv_s = reinterpret_cast<float*>(p + planes);
-    w.xsum = reinterpret_cast<float*>(p + planes + round256(B * 4));
-    (void)group_size;
+    p += planes;
+    w.inv_s = reinterpret_cast<float*>(p);
+    p += round256(B * 4);
+    w.xsum = reinterpret_cast<float*>(p);
+    p += round256(ngroups_of(K, group_size) * bpad_of(B) * 4);
+    w.part = reinterpret_cast<float*>(p);
+    if (w.plan.splits > 1) p += round256((int64_t)w.plan.splits * w.tiles * bn * BM * 4);
+    w.counters = reinterpret_cast<int*>(p);
     return w;
 }
 
-template <int BN, int NS, int BITS>
-cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s) {
+template <int BN, int NS, int BITS, bool SPLIT>
+cudaError_t launch_bn_t(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s) {
     using L = Smem<BN, NS, BITS>;
     CUtensorMap mq;
     if (!encode_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.q, (uint64_t)g.q_stride, (uint64_t)g.M,
@@ -844,6 +941,10 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.n_extra = g.n_extra;
     p.y_all = g.y_all;
     p.bias = g.bias;
+    p.part = w.part;
+    p.counters = w.counters;
+    p.splits = w.plan.splits;
+    p.gran = w.plan.gran;
     for (int d = 0; d < 7; ++d) p.y_extra[d] = g.y_extra[d];
     p.fault = fault_word();
     if (p.fault == nullptr) return cudaErrorInvalidDevicePointer;
@@ -858,7 +959,7 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     p.tiles_n = (int)((g.B + BN - 1) / BN);
     p.ldy = g.ldy;
     const size_t smem = (size_t)L::TOTAL + 1024;
-    auto kern = dq_gemm_tc_kernel<BN, NS, BITS>;
+    auto kern = dq_gemm_tc_kernel<BN, NS, BITS, SPLIT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     // the setmaxnreg split assumes the launch gives every thread exactly
@@ -870,8 +971,15 @@ cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s
     if (attr.numRegs != Cfg<BN>::LAUNCH_REGS) return cudaErrorInvalidConfiguration;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    kern<<<(unsigned)grid, Cfg<BN>::THREADS, smem, s>>>(p, mq);
+    kern<<<dim3((unsigned)grid, (unsigned)p.splits), Cfg<BN>::THREADS, smem, s>>>(p, mq);
     return cudaGetLastError();
+}
+
+// the split-K epilogue is a separate instantiation, so the unsplit kernel
+// (large batches) keeps its register allocation
+template <int BN, int NS, int BITS>
+cudaError_t launch_bn(const GemmProblem& g, const TcWorkspace& w, cudaStream_t s) {
+    return w.plan.splits > 1 ? launch_bn_t<BN, NS, BITS, true>(g, w, s) : launch_bn_t<BN, NS, BITS, false>(g, w, s);
 }
 
 }  // namespace
@@ -885,20 +993,26 @@ bool tc_supported(const GemmProblem& p) {
     return encode_fn() != nullptr;
 }
 
-size_t tc_workspace_bytes(int64_t B, int64_t K, int group_size) {
-    // fp16 hi + lo planes of the padded batch, 1/S_b, per-group sums of x' S_b
-    return (size_t)(bpad_of(B) * kt_of(K) * BK * 4 + round256(B * 4) + ngroups_of(K, group_size) * bpad_of(B) * 4 +
-                    256);
+size_t tc_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
+    // fp16 hi + lo planes of the padded batch, 1/S_b, per-group sums of x' S_b,
+    // and for split-K the partial tiles and one counter per output tile
+    const SplitPlan sp = split_plan(B, M, K, group_size, bits);
+    const int bn = bn_of(B);
+    const int64_t tiles = ((M + BM - 1) / BM) * ((B + bn - 1) / bn);
+    int64_t bytes = bpad_of(B) * kt_of(K) * BK * 4 + round256(B * 4) + round256(ngroups_of(K, group_size) * bpad_of(B) * 4);
+    if (sp.splits > 1) bytes += round256((int64_t)sp.splits * tiles * bn * BM * 4);
+    return (size_t)(bytes + round256(tiles * 4) + 256);
 }
 
 cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
-    const TcWorkspace w = carve(workspace, g.B, g.K, g.group_size);
+    const TcWorkspace w = carve(workspace, g.B, g.M, g.K, g.group_size, g.bits);
     const int bn = bn_of(g.B);
     const int64_t bpad = bpad_of(g.B);
     const int64_t ng = ngroups_of(g.K, g.group_size);
     const int gsz = ng == 1 ? (int)g.K : g.group_size;
     prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn,
-                                                 g.bits == 4, w.planes, w.inv_s, gsz, (int)ng, (int)bpad, w.xsum);
+                                                 g.bits == 4, w.planes, w.inv_s, gsz, (int)ng, (int)bpad, w.xsum,
+                                                 w.counters, w.plan.splits > 1 ? (int)w.tiles : 0);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // x' stage counts: 192 KB of planes next to two 16 KB codes stages

@@ -148,6 +148,13 @@ __global__ void __launch_bounds__(kImmaThreads, 1) gemv_imma_kernel(const ImmaPa
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const bool producer = warp == kImmaWarps;
+    // Programmatic dependent launch: the next kernel on the stream may be
+    // scheduled now (its CTAs take an SM as ours leave it, and run up to their
+    // own wait), and this one reads nothing in global memory before every
+    // earlier kernel on the stream has completed and its writes are visible.
+    // Without the launch attribute both instructions do nothing.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n_blocks = (p.M + p.rb - 1) / p.rb;
     const uint32_t full0 = smem_addr(full);
     const uint32_t cons0 = smem_addr(consumed);
@@ -654,8 +661,20 @@ cudaError_t launch_imma_t(ImmaParams p, size_t smem, cudaStream_t s) {
     const int n_blocks = (p.M + p.rb - 1) / p.rb;
     int grid = grid_max < n_blocks ? grid_max : n_blocks;
     if (grid < 1) grid = 1;
-    kern<<<grid, kImmaThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    // launched with programmatic stream serialization (see the kernel's first
+    // lines): back-to-back decode layers overlap one launch's start with the
+    // previous kernel's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kImmaThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int NB>

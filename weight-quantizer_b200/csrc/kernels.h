@@ -43,10 +43,12 @@ cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
 
 // --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
 // Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
-// single group). Workspace: the fp16 hi/lo planes of x', 1/S_b and the
-// per-group sums of x' (for zero points that are not integers).
+// single group). Workspace: the fp16 hi/lo planes of x', 1/S_b, the
+// per-group sums of x' (for zero points that are not integers) and, when
+// the output tiles are too few to fill the GPU, split-K partial tiles and
+// arrival counters.
 bool tc_supported(const GemmProblem& p);
-size_t tc_workspace_bytes(int64_t B, int64_t K, int group_size);
+size_t tc_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits);
 cudaError_t launch_tc(const GemmProblem& p, void* workspace, cudaStream_t s);
 
 // --- generic tiled SIMT kernel: any shape, reference per-element formula ---

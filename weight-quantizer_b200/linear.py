@@ -1,10 +1,17 @@
-"""Drop-in quantized replacement for nn.Linear and GPT-2 Conv1D (mirror of src/ptqkit/linear.py).
+"""``QuantizedLinear``: a Linear / GPT-2 Conv1D whose weight stays quantized on the GPU.
 
-Forward is y = x @ W_hat^T + bias with W_hat the dequantized integer weight.
-``impl="kernel"`` calls the sm_100a dequant-GEMM on the stored codes;
-``impl="reference"`` the dense reconstruction + matmul. ``materialize`` caches
-W_hat so a later forward is a plain fp32 GEMM; ``_apply`` (device moves)
-clears that cache, as in the reference (linear.py:77-88).
+The module holds ptqkit's storage (``QuantizedWeight``: codes, scales, zeros,
+optional AWQ channel scale) as buffers with ptqkit's names, which is what the
+compressed on-disk format (src/ptqkit/convert.py:296-336) keys on, and
+computes ``y = x @ W_hat^T + bias``:
+
+* ``impl="kernel"``: the sm_100a dequant-GEMM straight from the stored codes,
+  with the bias added in the kernel's epilogue (the same single fp32 add as
+  ptqkit's ``y + bias``, src/ptqkit/linear.py:99-100);
+* ``impl="reference"``: ptqkit's dense formulation, W_hat then a matmul.
+
+``materialize()`` keeps a dense W_hat so later calls are one fp32 GEMM (what
+ptqkit's sequential calibration relies on); moving the module drops it.
 """
 
 from __future__ import annotations
@@ -16,99 +23,74 @@ import torch
 from torch import nn
 
 from .gemm import dequant_gemm
-from .quant import Granularity, QuantizedWeight
+from .quant import QuantizedWeight, dequantize_weight
+
+_IMPLS = ("reference", "kernel")
+# QuantizedWeight fields that are plain metadata (the tensors become buffers)
+_META = ("bits", "group_size", "in_features", "out_features", "symmetric", "packed", "granularity")
 
 
 class QuantizedLinear(nn.Module):
+    """Linear layer over a ``QuantizedWeight`` (see the module docstring)."""
+
     codes: torch.Tensor
     scales: torch.Tensor
     zeros: torch.Tensor
-    bias: torch.Tensor | None
     channel_scale: torch.Tensor | None
+    bias: torch.Tensor | None
 
-    def __init__(
-        self,
-        qw: QuantizedWeight,
-        bias: torch.Tensor | None,
-        *,
-        impl: str = "reference",
-    ) -> None:
+    def __init__(self, qw: QuantizedWeight, bias: torch.Tensor | None, *, impl: str = "reference") -> None:
         super().__init__()
-        if impl not in ("reference", "kernel"):
+        if impl not in _IMPLS:
             raise ValueError("impl must be 'reference' or 'kernel'")
-        self.in_features = qw.in_features
-        self.out_features = qw.out_features
-        self.bits = qw.bits
-        self.group_size = qw.group_size
-        self.symmetric = qw.symmetric
-        self.packed = qw.packed
-        self.granularity: Granularity = qw.granularity
         self.impl = impl
-        self.awq_alpha: float | None = None
-        self._cached: torch.Tensor | None = None
-        self.register_buffer("codes", qw.codes.detach().contiguous())
-        self.register_buffer("scales", qw.scales.detach().contiguous())
-        self.register_buffer("zeros", qw.zeros.detach().contiguous())
-        if qw.channel_scale is not None:
-            self.register_buffer("channel_scale", qw.channel_scale.detach().contiguous())
-        else:
-            self.channel_scale = None
+        self.awq_alpha: float | None = None   # set by the AWQ calibration
+        self._meta: dict[str, Any] = {k: getattr(qw, k) for k in _META}
+        for name in ("codes", "scales", "zeros", "channel_scale"):
+            t = getattr(qw, name)
+            self.register_buffer(name, None if t is None else t.detach().contiguous())
         if bias is not None:
-            if int(bias.numel()) != qw.out_features:
+            b = bias.detach().to(dtype=torch.float32).reshape(-1).contiguous()
+            if int(b.numel()) != qw.out_features:
                 raise ValueError("bias does not match out_features")
-            self.register_buffer(
-                "bias", bias.detach().to(device=qw.codes.device, dtype=torch.float32).contiguous()
-            )
-        else:
-            self.bias = None
+            bias = b
+        self.register_buffer("bias", bias)
+        self._dense: torch.Tensor | None = None
+
+    def __getattr__(self, name: str) -> Any:
+        meta = self.__dict__.get("_meta")
+        if meta is not None and name in meta:
+            return meta[name]
+        return super().__getattr__(name)
 
     def quantized_weight(self) -> QuantizedWeight:
-        return QuantizedWeight(
-            codes=self.codes,
-            scales=self.scales,
-            zeros=self.zeros,
-            bits=self.bits,
-            group_size=self.group_size,
-            in_features=self.in_features,
-            out_features=self.out_features,
-            symmetric=self.symmetric,
-            packed=self.packed,
-            granularity=self.granularity,
-            channel_scale=self.channel_scale,
-        )
+        return QuantizedWeight(codes=self.codes, scales=self.scales, zeros=self.zeros,
+                               channel_scale=self.channel_scale, **self._meta)
 
     def materialize(self) -> None:
-        from .quant import dequantize_weight
-
-        self._cached = dequantize_weight(self.quantized_weight())
+        """Keep the dense reconstruction W_hat; forward becomes one fp32 GEMM."""
+        self._dense = dequantize_weight(self.quantized_weight())
 
     def clear_cache(self) -> None:
-        self._cached = None
+        self._dense = None
 
     def _apply(self, fn: Callable[..., Any], recurse: bool = True) -> QuantizedLinear:
-        self._cached = None
+        self._dense = None   # a moved or cast module rebuilds W_hat on demand
         super()._apply(fn, recurse=recurse)  # type: ignore[no-untyped-call]
         return self
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.shape[-1] != self.in_features:
-            raise ValueError(f"expected in_features={self.in_features}, got {x.shape[-1]}")
-        lead = x.shape[:-1]
-        flat = x.reshape(-1, self.in_features)
-        if self._cached is not None:
-            y = nn.functional.linear(flat, self._cached, self.bias)
-        elif self.impl == "kernel":
-            # the bias add (linear.py:99-100) happens in the kernel's epilogue
-            y = dequant_gemm(flat, self.quantized_weight(), impl="kernel", bias=self.bias)
-        else:
-            y = dequant_gemm(flat, self.quantized_weight(), impl=self.impl)
-            if self.bias is not None:
-                y = y + self.bias
-        return y.reshape(*lead, self.out_features)
+        n_in = self._meta["in_features"]
+        if x.shape[-1] != n_in:
+            raise ValueError(f"expected in_features={n_in}, got {x.shape[-1]}")
+        if self._dense is not None:
+            flat = x.reshape(-1, n_in)
+            y = nn.functional.linear(flat, self._dense, self.bias)
+            return y.reshape(*x.shape[:-1], self._meta["out_features"])
+        return dequant_gemm(x, self.quantized_weight(), impl=self.impl, bias=self.bias)
 
     def extra_repr(self) -> str:
-        alpha = "" if self.awq_alpha is None else f", awq_alpha={self.awq_alpha}"
-        return (
-            f"in={self.in_features}, out={self.out_features}, bits={self.bits}, "
-            f"group={self.group_size}, sym={self.symmetric}, impl={self.impl}{alpha}"
-        )
+        m = self._meta
+        tail = "" if self.awq_alpha is None else f", awq_alpha={self.awq_alpha}"
+        return (f"in={m['in_features']}, out={m['out_features']}, bits={m['bits']}, group={m['group_size']}, "
+                f"sym={m['symmetric']}, impl={self.impl}{tail}")
