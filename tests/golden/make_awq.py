@@ -1,8 +1,8 @@
 """Generate the AWQ golden fixtures from the reference itself.
 
-Run where the ptqkit reference tree is mounted (default /root/reference):
+Run where the ptqkit reference tree is mounted (the --reference argument or WQ_REFERENCE_ROOT):
 
-    python tests/golden/make_awq.py [--reference /root/reference]
+    python tests/golden/make_awq.py [--reference <ptqkit tree>]   (or WQ_REFERENCE_ROOT=<ptqkit tree>)
 
 For each case, the inputs are seeded CPU tensors, and the outputs come from
 ptqkit's own code: ``ptqkit.awq.awq_quantize`` gives the winning alpha and the
@@ -86,8 +86,11 @@ def cases() -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("WQ_REFERENCE_ROOT"),
+                    help="ptqkit source tree (default: $WQ_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set WQ_REFERENCE_ROOT to the ptqkit source tree")
     sys.path.insert(0, os.path.join(args.reference, "src"))
     awq = importlib.import_module("ptqkit.awq")
     quant = importlib.import_module("ptqkit.quant")

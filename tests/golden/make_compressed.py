@@ -1,9 +1,9 @@
 """Generate the compressed-format fixtures from the reference itself.
 
-Run where the ptqkit reference tree is mounted (default /root/reference),
+Run where the ptqkit reference tree is mounted (the --reference argument or WQ_REFERENCE_ROOT),
 after ``make -C oracle ref`` built its C++ kernel:
 
-    python tests/golden/make_compressed.py [--reference /root/reference]
+    python tests/golden/make_compressed.py [--reference <ptqkit tree>]   (or WQ_REFERENCE_ROOT=<ptqkit tree>)
 
 For each case below a ``CompressedNet`` (defined here; the tests import this
 file for the class) is built from a seed, quantized by ptqkit's
@@ -120,8 +120,11 @@ def load_reference(ref_root: str):  # type: ignore[no-untyped-def]
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("WQ_REFERENCE_ROOT"),
+                    help="ptqkit source tree (default: $WQ_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set WQ_REFERENCE_ROOT to the ptqkit source tree")
     load_reference(args.reference)
     from ptqkit.convert import (
         matrix_nbytes,

@@ -1,9 +1,9 @@
 """Generate the golden fixtures from the reference itself.
 
 Run in a checkout where the ptqkit reference tree is mounted (default
-/root/reference) after ``make -C oracle ref`` built its C++ kernel:
+WQ_REFERENCE_ROOT) after ``make -C oracle ref`` built its C++ kernel:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <ptqkit tree>]   (or WQ_REFERENCE_ROOT=<ptqkit tree>)
 
 Writes, next to this script:
 
@@ -60,9 +60,12 @@ def load_reference(ref_root: str):  # type: ignore[no-untyped-def]
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("WQ_REFERENCE_ROOT"),
+                    help="ptqkit source tree (default: $WQ_REFERENCE_ROOT)")
     ap.add_argument("--skip-workloads", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set WQ_REFERENCE_ROOT to the ptqkit source tree")
     ptq, kern = load_reference(args.reference)
     from ptqkit.gemm import dequant_gemm as ref_gemm
     from ptqkit.pack import pack_int4 as ref_pack

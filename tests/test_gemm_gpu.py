@@ -177,19 +177,15 @@ def test_output_into_strided_view(wq, cuda) -> None:
 def test_workloads_vs_oracle(wq, orc, cuda, wname: str) -> None:
     wl = importlib.import_module("weight-quantizer_b200.workloads")
     layers = wl.WORKLOADS[wname]()
-    dig = workload_digests()[wname]
-    sample = torch.Generator().manual_seed(3)
-    for layer, d in zip(layers, dig):
+    assert len(layers) == len(workload_digests()[wname])
+    for layer in layers:
         qw = wq.quantize_weight(layer.weight, layer.config, pre_scale=layer.pre_scale)
         for b, x in layer.x.items():
             got = wq.dequant_gemm(x.to(cuda), qw, impl="kernel").cpu()
-            if b <= 256:
-                ref = _oracle_y(orc, qw, x)
-                assert_close_y(got.numpy(), ref, f"{wname}/{layer.name} b{b}")
-            else:
-                rows = torch.randperm(b, generator=sample)[:64]
-                ref = _oracle_y(orc, qw, x[rows])
-                assert_close_y(got[rows].numpy(), ref, f"{wname}/{layer.name} b{b} sampled rows")
+            # every row, batch 4096 of the 28672 x 8192 layer included (the
+            # oracle's threads take a few seconds for it)
+            ref = _oracle_y(orc, qw, x)
+            assert_close_y(got.numpy(), ref, f"{wname}/{layer.name} b{b}")
 
 
 @pytest.mark.parametrize("batch", [5, 64, 4096])
