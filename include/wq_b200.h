@@ -238,9 +238,8 @@ WQ_API int wq_sq_err_sum_f64(const float* a, const float* b, int64_t n, double* 
 
 /* ------------------------------------------------------------------------ */
 /* GPTQ column sweep (src/ptqkit/gptq.py:86-191), fp64. The caller factors   */
-/* the damped inverse Hessian (gptq.py:44-71) and applies each block's       */
-/* update of the later columns as one GEMM (gptq.py:124-125); these are the  */
-/* per-row parts.                                                            */
+/* the damped inverse Hessian (gptq.py:44-71); these are the per-row sweep   */
+/* and each block's update of the later columns (gptq.py:124-125).           */
 /* ------------------------------------------------------------------------ */
 /* Grid of quant.py:146-172 in fp64 over columns [c0, c1) of w (fp64 [rows,  */
 /* ld]): per row (per_tensor = 0; scale_out/zero_out[r * out_stride]) or for */
@@ -258,9 +257,22 @@ WQ_API int wq_gptq_qparams_f64(const double* w, int64_t rows, int64_t ld, int64_
 /* U = hinv (fp64 [K, ldh], upper Cholesky factor of the damped inverse), in */
 /* the reference's operation order. Writes int32 codes[r * ldc + s0 + i] and  */
 /* the errors err_block (fp64 [rows, count]); w is read only. count <= 128.   */
+/* zero_err (uint8 [count] or NULL): columns whose error is taken as 0 for    */
+/* every row, as _obs_block does when a column's error is not finite          */
+/* (gptq.py:114-115). bad_col (int32 device word or NULL; the caller sets it  */
+/* to INT32_MAX): receives the first column, not masked, whose error is not   */
+/* finite in some row; the caller then sweeps the block again with that       */
+/* column masked.                                                             */
 WQ_API int wq_gptq_block_f64(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh,
                              int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
-                             int bits, int32_t* codes, int64_t ldc, double* err_block, void* stream);
+                             int bits, int32_t* codes, int64_t ldc, double* err_block, const uint8_t* zero_err,
+                             int32_t* bad_col, void* stream);
+/* The tail update after one block (gptq.py:124-125), fp64:                   */
+/* w[r, c0 + j] -= sum_i err_block[r, i] * hinv[s0 + i, c0 + j] for j < ncols,  */
+/* i < count; the sum in i order, then one subtraction.                       */
+WQ_API int wq_gptq_tail_f64(double* w, int64_t rows, int64_t ld, int64_t c0, int64_t ncols,
+                            const double* err_block, int count, const double* hinv, int64_t ldh, int64_t s0,
+                            void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */

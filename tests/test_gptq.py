@@ -73,8 +73,12 @@ def test_gptq_entry_point_validation(wq) -> None:
     assert lib.wq_gptq_qparams_f64(d, 2, 3, 0, 4, 4, 1, 0, d, d, 1, None, 0, None) == 20
     assert lib.wq_gptq_qparams_f64(d, 2, 4, 0, 4, 4, 1, 1, d, d, 1, None, 0, None) == 12
     assert lib.wq_gptq_qparams_f64(None, 2, 4, 0, 4, 4, 1, 0, d, d, 1, None, 0, None) == 11
-    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 129, d, d, 1, 4, d, 256, d, None) == 13
-    assert lib.wq_gptq_block_f64(d, 2, 64, d, 256, 0, 128, d, d, 1, 4, d, 256, d, None) == 20
-    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 64, d, d, 1, 8, None, 256, d, None) == 11
-    assert lib.wq_gptq_block_f64(d, -2, 256, d, 256, 0, 64, d, d, 1, 8, d, 256, d, None) == 5
-    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 64, d, d, 1, 6, d, 256, d, None) == 3
+    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 129, d, d, 1, 4, d, 256, d, None, None, None) == 13
+    assert lib.wq_gptq_block_f64(d, 2, 64, d, 256, 0, 128, d, d, 1, 4, d, 256, d, None, None, None) == 20
+    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 64, d, d, 1, 8, None, 256, d, None, None, None) == 11
+    assert lib.wq_gptq_block_f64(d, -2, 256, d, 256, 0, 64, d, d, 1, 8, d, 256, d, None, None, None) == 5
+    assert lib.wq_gptq_block_f64(d, 2, 256, d, 256, 0, 64, d, d, 1, 6, d, 256, d, None, None, None) == 3
+    # the tail update: negative sizes, short strides, null pointers
+    assert lib.wq_gptq_tail_f64(d, -1, 8, 0, 8, d, 4, d, 8, 0, None) == 5
+    assert lib.wq_gptq_tail_f64(d, 2, 8, 4, 8, d, 4, d, 16, 0, None) == 20
+    assert lib.wq_gptq_tail_f64(None, 2, 16, 4, 8, d, 4, d, 16, 0, None) == 11

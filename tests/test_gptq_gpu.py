@@ -145,3 +145,28 @@ def test_quantize_model_gptq_tiny_mlp(wq, cuda, sequential: bool) -> None:
     r = oracle.gptq_quantize(w1, x.T @ x / x.shape[0], 4, True, 8, 0.01, 128)
     got = oracle.unpack_int4(model.fc1.codes.cpu().numpy(), 16).astype(np.int32)
     assert (got != r["codes"]).mean() <= 0.01
+
+
+@pytest.mark.parametrize("group", [32, None])
+def test_nonfinite_obs_error_zeroes_the_column(wq, cuda, monkeypatch, group: int | None) -> None:
+    """_obs_block (gptq.py:114-115) zeroes a column's OBS error in every row when
+    any row's is not finite. A NaN planted on one diagonal entry of the factor
+    (and, for the grouped case, a second one in a later block) makes that
+    column's error NaN; the device sweep must give the oracle's codes bit for
+    bit, i.e. zero those columns' errors and carry on."""
+    g = torch.Generator().manual_seed(77)
+    k = 192
+    x = torch.randn(3 * k, k, generator=g)
+    w = torch.randn(24, k, generator=g) * 0.05
+    h = x.double().transpose(0, 1) @ x.double() / x.shape[0]
+    mod = gptq_mod()
+    u = mod._factor_inverse(h.to(cuda), 0.01).clone()
+    u[7, 7] = float("nan")
+    u[150, 150] = float("nan")
+    monkeypatch.setattr(mod, "_factor_inverse", lambda hess, percdamp: u)
+    cfg = wq.QuantConfig(bits=4, symmetric=True, group_size=group, method=wq.Method.GPTQ, percdamp=0.01,
+                         blocksize=128)
+    qw = mod.gptq_quantize(w.to(cuda), h.to(cuda), cfg)
+    r = oracle.gptq_quantize(w.numpy(), h.numpy(), 4, True, group, 0.01, 128, hinv=u.cpu().numpy())
+    assert np.array_equal(unpacked(qw.codes.cpu().numpy(), 4, k), r["codes"])
+    assert np.isfinite(qw.scales.cpu().numpy()).all()

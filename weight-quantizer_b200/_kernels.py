@@ -73,7 +73,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_sq_err_sum_f64": (_int, [_vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "wq_gptq_qparams_workspace_bytes": (_sz, [_i64]),
     "wq_gptq_qparams_f64": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _i64, _vp, _sz, _vp]),
-    "wq_gptq_block_f64": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _vp, _i64, _int, _vp, _i64, _vp, _vp]),
+    "wq_gptq_block_f64": (
+        _int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _vp, _i64, _int, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "wq_gptq_tail_f64": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _i64, _vp]),
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
@@ -604,9 +606,13 @@ def gptq_qparams(w: torch.Tensor, c0: int, c1: int, bits: int, symmetric: bool, 
 
 
 def gptq_block(w: torch.Tensor, hinv: torch.Tensor, s0: int, count: int, scale: torch.Tensor,
-               zero: torch.Tensor, qp_stride: int, bits: int, codes: torch.Tensor, err_block: torch.Tensor) -> None:
+               zero: torch.Tensor, qp_stride: int, bits: int, codes: torch.Tensor, err_block: torch.Tensor,
+               zero_err: torch.Tensor | None = None, bad_col: torch.Tensor | None = None) -> None:
     """_obs_block's column sweep over [s0, s0 + count) (gptq.py:86-121): writes
-    codes[:, s0:s0 + count] and the OBS errors into err_block [rows, count]."""
+    codes[:, s0:s0 + count] and the OBS errors into err_block [rows, count].
+    ``zero_err`` (uint8 [count]) marks columns whose error counts as 0;
+    ``bad_col`` (int32 [1], preset to 2^31 - 1) receives the first other
+    column whose error is not finite in some row."""
     dev = _cuda_device([w, hinv, scale, zero, codes, err_block])
     for t in (w, hinv, scale, zero, err_block):
         if t.dtype != torch.float64:
@@ -615,5 +621,18 @@ def gptq_block(w: torch.Tensor, hinv: torch.Tensor, s0: int, count: int, scale: 
         raise ValueError("codes must be int32; w, hinv row-major; err_block contiguous")
     _check(library().wq_gptq_block_f64(_ptr(w), int(w.shape[0]), int(w.stride(0)), _ptr(hinv), int(hinv.stride(0)),
                                        int(s0), int(count), _ptr(scale), _ptr(zero), int(qp_stride), int(bits),
-                                       _ptr(codes), int(codes.stride(0)), _ptr(err_block), _stream(dev)))
+                                       _ptr(codes), int(codes.stride(0)), _ptr(err_block), _ptr(zero_err),
+                                       _ptr(bad_col), _stream(dev)))
+
+
+def gptq_tail(w: torch.Tensor, c0: int, err_block: torch.Tensor, hinv: torch.Tensor, s0: int) -> None:
+    """w[:, c0:] -= err_block @ hinv[s0:s0 + count, c0:] in fp64 (gptq.py:124-125),
+    this library's kernel, the sum over the block's columns in order."""
+    dev = _cuda_device([w, err_block, hinv])
+    rows, count = int(err_block.shape[0]), int(err_block.shape[1])
+    ncols = int(w.shape[1]) - int(c0)
+    if not err_block.is_contiguous() or w.stride(1) != 1 or hinv.stride(1) != 1:
+        raise ValueError("err_block contiguous; w, hinv row-major")
+    _check(library().wq_gptq_tail_f64(_ptr(w), rows, int(w.stride(0)), int(c0), ncols, _ptr(err_block), count,
+                                      _ptr(hinv), int(hinv.stride(0)), int(s0), _stream(dev)))
 

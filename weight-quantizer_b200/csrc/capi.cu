@@ -507,7 +507,8 @@ int wq_gptq_qparams_f64(const double* w, int64_t rows, int64_t ld, int64_t c0, i
 
 int wq_gptq_block_f64(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh, int64_t s0,
                       int count, const double* scale, const double* zero, int64_t qp_stride, int bits,
-                      int32_t* codes, int64_t ldc, double* err_block, void* stream) {
+                      int32_t* codes, int64_t ldc, double* err_block, const uint8_t* zero_err, int32_t* bad_col,
+                      void* stream) {
     if (rows < 0 || s0 < 0 || count < 0 || qp_stride < 0) return WQ_E_NEG_DIM;
     if (bits != 4 && bits != 8) return WQ_E_BITS;
     if (count > wq::gptq_max_block() || rows > kMaxDim) return WQ_E_TOO_LARGE;
@@ -517,7 +518,19 @@ int wq_gptq_block_f64(const double* w, int64_t rows, int64_t ld, const double* h
         err_block == nullptr)
         return WQ_E_NULL;
     cudaError_t e = wq::launch_gptq_block(w, rows, ld, hinv, ldh, s0, count, scale, zero, qp_stride, bits, codes, ldc,
-                                          err_block, static_cast<cudaStream_t>(stream));
+                                          err_block, zero_err, bad_col, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
+int wq_gptq_tail_f64(double* w, int64_t rows, int64_t ld, int64_t c0, int64_t ncols, const double* err_block,
+                     int count, const double* hinv, int64_t ldh, int64_t s0, void* stream) {
+    if (rows < 0 || c0 < 0 || ncols < 0 || count < 0 || s0 < 0) return WQ_E_NEG_DIM;
+    if (ld < c0 + ncols || ldh < c0 + ncols) return WQ_E_LD;
+    if (rows == 0 || ncols == 0 || count == 0) return WQ_OK;
+    if (w == nullptr || err_block == nullptr || hinv == nullptr) return WQ_E_NULL;
+    if ((rows + 63) / 64 > 65535) return WQ_E_TOO_LARGE;
+    cudaError_t e = wq::launch_gptq_tail(w, rows, ld, c0, ncols, err_block, count, hinv, ldh, s0,
+                                         static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 

@@ -128,7 +128,8 @@ __global__ void qparams_tensor_kernel(const double* __restrict__ partial, int64_
 __global__ void __launch_bounds__(kGptqWarps * 32) gptq_block_kernel(
     const double* __restrict__ w, int64_t rows, int64_t ld, const double* __restrict__ hinv, int64_t ldh,
     int64_t s0, int count, const double* __restrict__ scale, const double* __restrict__ zero, int64_t qp_stride,
-    int qmax, int32_t* __restrict__ codes, int64_t ldc, double* __restrict__ err_block) {
+    int qmax, int32_t* __restrict__ codes, int64_t ldc, double* __restrict__ err_block,
+    const uint8_t* __restrict__ zero_err, int* __restrict__ bad_col) {
     extern __shared__ double h_s[];   // [count][count]: U[s0 + i][s0 + j]
     for (int idx = threadIdx.x; idx < count * count; idx += blockDim.x) {
         const int i = idx / count, j = idx - i * count;
@@ -161,7 +162,16 @@ __global__ void __launch_bounds__(kGptqWarps * 32) gptq_block_kernel(
             q = q < 0.0 ? 0.0 : (q > (double)qmax ? (double)qmax : q);
             const double deq = __dmul_rn(sc, __dsub_rn(q, zz));
             const double d = h_s[i * count + i];
-            const double err = __ddiv_rn(__dsub_rn(col, deq), d < 1e-8 ? 1e-8 : d);
+            double err = __ddiv_rn(__dsub_rn(col, deq), d < 1e-8 ? 1e-8 : d);
+            // _obs_block zeroes a column's whole error when any row's is not
+            // finite (gptq.py:114-115). A row cannot see the other rows here,
+            // so the first such column is reported and the caller sweeps the
+            // block again with that column's error set to zero.
+            if (zero_err != nullptr && zero_err[i] != 0) {
+                err = 0.0;
+            } else if (bad_col != nullptr && !isfinite(err) && lane == l) {
+                atomicMin(bad_col, i);
+            }
             if (lane == l) {
                 crow[i] = (int32_t)q;
                 erow[i] = err;
@@ -176,7 +186,67 @@ __global__ void __launch_bounds__(kGptqWarps * 32) gptq_block_kernel(
     }
 }
 
+// work[r, c0 + j] -= sum_i err[r, i] * hinv[s0 + i, c0 + j]: the tail update
+// after one block (gptq.py:124-125), a 64 x 64 output tile per CTA, 4 x 4 per
+// thread, the i sum in order (deterministic), then one subtraction.
+constexpr int kTailT = 64, kTailK = 16;
+__global__ void __launch_bounds__(256) gptq_tail_kernel(double* __restrict__ work, int64_t rows, int64_t ld, int64_t c0,
+                                                        int64_t ncols, const double* __restrict__ err, int count,
+                                                        const double* __restrict__ hinv, int64_t ldh, int64_t s0) {
+    __shared__ double es[kTailK][kTailT + 1];   // err^T tile: [i][row]
+    __shared__ double hs[kTailK][kTailT];       // hinv tile: [i][col]
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int64_t r0 = (int64_t)blockIdx.y * kTailT, j0 = (int64_t)blockIdx.x * kTailT;
+    double acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0;
+    for (int k0 = 0; k0 < count; k0 += kTailK) {
+        for (int idx = threadIdx.x; idx < kTailK * kTailT; idx += 256) {
+            const int kk = idx % kTailK, rr = idx / kTailK;   // consecutive threads walk i of one row
+            const int64_t r = r0 + rr;
+            es[kk][rr] = (r < rows && k0 + kk < count) ? err[r * count + k0 + kk] : 0.0;
+            const int cc = idx % kTailT, k2 = idx / kTailT;
+            const int64_t j = j0 + cc;
+            hs[k2][cc] = (j < ncols && k0 + k2 < count) ? hinv[(s0 + k0 + k2) * ldh + c0 + j] : 0.0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kTailK; ++kk) {
+            double ev[4], hv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) ev[a] = es[kk][ty * 4 + a];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) hv[b] = hs[kk][tx * 4 + b];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fma(ev[a], hv[b], acc[a][b]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int64_t r = r0 + ty * 4 + a;
+        if (r >= rows) continue;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int64_t j = j0 + tx * 4 + b;
+            if (j < ncols) work[r * ld + c0 + j] = __dsub_rn(work[r * ld + c0 + j], acc[a][b]);
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gptq_tail(double* work, int64_t rows, int64_t ld, int64_t c0, int64_t ncols, const double* err,
+                             int count, const double* hinv, int64_t ldh, int64_t s0, cudaStream_t s) {
+    if (rows == 0 || ncols == 0 || count == 0) return cudaSuccess;
+    const dim3 grid((unsigned)((ncols + kTailT - 1) / kTailT), (unsigned)((rows + kTailT - 1) / kTailT));
+    gptq_tail_kernel<<<grid, 256, 0, s>>>(work, rows, ld, c0, ncols, err, count, hinv, ldh, s0);
+    return cudaGetLastError();
+}
 
 size_t gptq_qparams_workspace_bytes(int64_t rows) { return (size_t)rows * 2 * sizeof(double); }
 
@@ -198,14 +268,15 @@ int gptq_max_block() { return kGptqBlock; }
 
 cudaError_t launch_gptq_block(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh,
                               int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
-                              int bits, int32_t* codes, int64_t ldc, double* err_block, cudaStream_t s) {
+                              int bits, int32_t* codes, int64_t ldc, double* err_block, const uint8_t* zero_err,
+                              int* bad_col, cudaStream_t s) {
     if (rows == 0 || count == 0) return cudaSuccess;
     const size_t smem = (size_t)count * count * sizeof(double);
     cudaError_t e = cudaFuncSetAttribute(gptq_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const unsigned grid = (unsigned)((rows + kGptqWarps - 1) / kGptqWarps);
     gptq_block_kernel<<<grid, kGptqWarps * 32, smem, s>>>(w, rows, ld, hinv, ldh, s0, count, scale, zero, qp_stride,
-                                                          (1 << bits) - 1, codes, ldc, err_block);
+                                                          (1 << bits) - 1, codes, ldc, err_block, zero_err, bad_col);
     return cudaGetLastError();
 }
 

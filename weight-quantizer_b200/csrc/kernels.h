@@ -103,7 +103,10 @@ cudaError_t launch_gptq_qparams(const double* w, int64_t rows, int64_t ld, int64
 int gptq_max_block();
 cudaError_t launch_gptq_block(const double* w, int64_t rows, int64_t ld, const double* hinv, int64_t ldh,
                               int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
-                              int bits, int32_t* codes, int64_t ldc, double* err_block, cudaStream_t s);
+                              int bits, int32_t* codes, int64_t ldc, double* err_block, const uint8_t* zero_err,
+                              int* bad_col, cudaStream_t s);
+cudaError_t launch_gptq_tail(double* work, int64_t rows, int64_t ld, int64_t c0, int64_t ncols, const double* err,
+                             int count, const double* hinv, int64_t ldh, int64_t s0, cudaStream_t s);
 
 // Number of SMs of the current device (cached per device).
 int sm_count();

@@ -13,14 +13,15 @@ factorization fails). Group scales come from the updated weights at the start
 of each group, per-channel and per-tensor scales once before the sweep.
 
 Device split: the factorization is cuSOLVER through torch.linalg (a plain
-library factorization); the per-row work runs in this library's kernels
-(``wq_gptq_qparams_f64``: the grid of quant.py:146-172 in fp64;
+library factorization, once per layer); the sweep runs in this library's
+kernels (``wq_gptq_qparams_f64``: the grid of quant.py:146-172 in fp64;
 ``wq_gptq_block_f64``: one block's column sweep, one warp per weight row,
-bit-exact with ptqkit's _obs_block given the same inputs); each block's
-update of the later columns is one fp64 GEMM (cuBLAS through torch). Groups
-wider than 128 columns are swept in 128-column blocks whose later columns are
-corrected by that GEMM, the same updates as the reference's per-column ones
-in a different summation order.
+bit-exact with ptqkit's _obs_block given the same inputs;
+``wq_gptq_tail_f64``: each block's update of the later columns, the
+O(K^2 M) part, an fp64 tile kernel summing in column order). Groups wider
+than 128 columns are swept in 128-column blocks whose later columns are
+corrected by that update, the same updates as the reference's per-column
+ones in a different summation order.
 
 Because the factorization and the GEMMs round differently from the CPU
 LAPACK/BLAS the reference runs on, codes agree with ptqkit's except where a
@@ -67,18 +68,36 @@ def _factor_inverse(hessian: torch.Tensor, percdamp: float) -> torch.Tensor:
     raise RuntimeError("damped Hessian Cholesky failed")
 
 
+_NO_BAD_COLUMN = 2**31 - 1
+
+
 def _sweep(work: torch.Tensor, hinv: torch.Tensor, codes: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor,
            qp_stride: int, bits: int, start: int, end: int) -> None:
     """Quantize columns [start, end) of ``work`` and correct the later columns
-    (gptq.py:86-125), in sweeps of at most 128 columns."""
+    (gptq.py:86-125), in sweeps of at most 128 columns.
+
+    A column whose OBS error is not finite in some row gets a zero error in
+    every row, as _obs_block does (gptq.py:114-115): the sweep kernel reports
+    the first such column and the block is swept again with it masked (the
+    sweep reads ``work`` without writing it, so a repeat starts clean)."""
     inn = int(work.shape[1])
     rows = int(work.shape[0])
+    bad = torch.empty(1, dtype=torch.int32, device=work.device)
     for s0 in range(start, end, _BLOCK):
         s1 = min(s0 + _BLOCK, end)
         err = torch.empty((rows, s1 - s0), dtype=torch.float64, device=work.device)
-        _kernels.gptq_block(work, hinv, s0, s1 - s0, scale, zero, qp_stride, bits, codes, err)
+        mask: torch.Tensor | None = None
+        for _ in range(s1 - s0 + 1):
+            bad.fill_(_NO_BAD_COLUMN)
+            _kernels.gptq_block(work, hinv, s0, s1 - s0, scale, zero, qp_stride, bits, codes, err, mask, bad)
+            col = int(bad.item())
+            if col == _NO_BAD_COLUMN:
+                break
+            if mask is None:
+                mask = torch.zeros(s1 - s0, dtype=torch.uint8, device=work.device)
+            mask[col] = 1
         if s1 < inn:
-            work[:, s1:] -= err @ hinv[s0:s1, s1:]
+            _kernels.gptq_tail(work, s1, err, hinv, s0)
 
 
 def gptq_quantize(weight: torch.Tensor, hessian: torch.Tensor, config: QuantConfig) -> QuantizedWeight:
