@@ -374,8 +374,30 @@ def config_lines(wq: Any, wl: Any, dev: Any, stream: Any, peaks: dict[str, Any],
                     "speedup_vs_cpu": round(cms_full / ms, 1),
                     "timed": "GPU RTN + pack and the host read of its status flags"})
         del wd
+    # GPTQ on a 4096 x 4096 int4 g128 layer (Hessian of 8192 calibration rows)
+    gq = importlib.import_module("weight-quantizer_b200.gptq")
+    g = torch.Generator().manual_seed(11)
+    kk = 4096
+    xc = torch.randn(8192, kk, generator=g)
+    hess = (xc.double().t() @ xc.double() / xc.shape[0])
+    wg = torch.randn(kk, kk, generator=g) * 0.02
+    gcfg = wq.QuantConfig(bits=4, symmetric=True, group_size=128, method=wq.Method.GPTQ)
+    hd, wd = hess.to(dev), wg.to(dev)
+    gms = gpu_ms(lambda: gq.gptq_quantize(wd, hd, gcfg))
+    sample_rows = 256
+    gms_sample = gpu_ms(lambda: gq.gptq_quantize(wd[:sample_rows], hd, gcfg))
+    gptq = {"layer": "4096x4096 int4 sym g128, Hessian of 8192 rows", "ms": round(gms, 2),
+            "timed": "factorization (cuSOLVER), qparams, sweep and tail kernels, host reads of their flags"}
+    if ref_rtn is not None:
+        ref_gptq = importlib.import_module("ptqkit.gptq")
+        rq = ref_rtn.QuantConfig(bits=4, symmetric=True, group_size=128, method=ref_rtn.Method.GPTQ)
+        ws = wg[:sample_rows].contiguous()
+        cms = cpu_ms(lambda: ref_gptq.gptq_quantize(ws, hess, rq), 0.0)
+        gptq["same_work"] = {"rows": sample_rows, "gpu_ms": round(gms_sample, 2), "cpu_ms": round(cms, 1),
+                             "cpu": f"ptqkit.gptq.gptq_quantize, torch CPU, {threads} threads",
+                             "speedup_vs_cpu": round(cms / gms_sample, 1)}
     del flush_w, flush_r
-    return {"configs": out, "rtn": rtn}
+    return {"configs": out, "rtn": rtn, "gptq": gptq}
 
 
 def ours(args: argparse.Namespace) -> None:
@@ -461,6 +483,25 @@ def ours(args: argparse.Namespace) -> None:
     value = flops / t_step / 1e9
     clock = clocks.summary()
 
+    # ---- N > 1: the same layer with y left sharded (no exchange) -------------
+    # the case where the next layer consumes the row shards (forward(gather=False))
+    no_gather = None
+    if world > 1:
+        for _ in range(args.warmup):
+            lin.forward(x, gather=False)
+        torch.cuda.synchronize()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.steps):
+            lin.forward(x, gather=False)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t_ng = max_over_ranks(s0.elapsed_time(s1) / args.steps / 1e3)
+        no_gather = {"value": round(flops / t_ng / 1e9, 1), "unit": "GFLOP/s", "ms_per_step": round(t_ng * 1e3, 4),
+                     "what": "each rank's row shard of y left in place (forward(gather=False)), max over ranks"}
+
     # ---- dominant kernel alone (local GEMM), for the roofline --------------
     local_out = torch.empty((max(batches), mp), dtype=torch.float32, device=dev)
     kt = []
@@ -477,7 +518,7 @@ def ours(args: argparse.Namespace) -> None:
     achieved_tflops = kernel_flops / t_kernel / 1e12
     # DRAM bytes (read + write) of one tensor-core launch at batch 4096 on one
     # GPU, from the ncu capture summarised in profiles/dq_gemm_tc_28672x8192_b4096.md
-    traffic = 2.848480e9 + 0.489388e9 if (B == 4096 and world == 1) else None
+    traffic = 2.828522e9 + 0.462504e9 if (B == 4096 and world == 1) else None
     roofline = {"bound": "tensor", "achieved": round(achieved_tflops, 3), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
                 "traffic_unit": "bytes per launch",
@@ -658,6 +699,7 @@ def ours(args: argparse.Namespace) -> None:
             "roofline": roofline,
             "sweep": sweep,
             "e2e": e2e,
+            "y_sharded": no_gather,
             "loader": loader,
             "per_config": per_config,
             "cpu_baseline": cpu,
