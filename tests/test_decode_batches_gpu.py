@@ -1,12 +1,15 @@
-"""Tensor-core dequant-GEMM at decode batches (5-32) against the oracle.
+"""Dequant-GEMM at decode batches (3-32) against the oracle.
 
-Batches 5-32 run the tcgen05 kernel with its narrowest batch tile. The cases
-cover every group layout it takes (g64, g128, g256, per-channel,
-per-tensor), odd and short K, row counts that are not multiples of 128,
-channel scales with outlier channels, fractional zero points, the bias
-epilogue and strided outputs; the 28672 x 8192 layer is checked on all rows.
-Tolerance: conftest.assert_close_y (max|dy| <= 1e-4 (1 + |y|), relative
-Frobenius <= 1e-5).
+Batches 3-32 run the integer tensor-core kernel with stream-K over units of
+256 rows x one fold block (dq_gemv_wide.cu). The cases cover every group
+layout it takes (g64, g128, g256, per-channel, per-tensor; tables by TMA box
+or by direct loads), int4 and int8, odd and short K, row counts that are not
+multiples of 256, layers small enough that every row block is shared by many
+CTAs (the fixed-order fix-up), channel scales with outlier channels,
+fractional zero points, the bias epilogue and strided outputs; the
+28672 x 8192 layer is checked on all rows. Batches just above 32 run the
+tcgen05 kernel, split-K on small layers. Tolerance: conftest.assert_close_y
+(max|dy| <= 1e-4 (1 + |y|), relative Frobenius <= 1e-5).
 """
 
 from __future__ import annotations
@@ -48,7 +51,7 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("batch", [5, 8, 16, 17, 32])
+@pytest.mark.parametrize("batch", [3, 5, 8, 16, 17, 25, 32, 33, 64])
 def test_decode_batches_vs_oracle(wq, orc, cuda, batch: int) -> None:
     g = torch.Generator().manual_seed(900 + batch)
     for (M, K, bits, sym, group, pre) in CASES:

@@ -173,10 +173,17 @@ int wq_selftest_expired_wait(uint32_t max_polls, void* stream) {
 
 size_t wq_dequant_gemm_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits) {
     if (B <= 0 || K <= 0 || group_size <= 0 || (bits != 4 && bits != 8)) return 0;
-    if (B <= wq::kGemvMaxBatch) return wq::gemv_workspace_bytes(B, K, bits);
-    const bool single_group = group_size >= K;
-    if (single_group || group_size % 64 == 0) return wq::tc_workspace_bytes(B, M, K, group_size, bits);
-    return 0;
+    // the larger of the two paths a problem of this size can take (which one
+    // runs also depends on the pointers' alignment)
+    size_t need = 0;
+    if (B <= wq::kGemvMaxBatch) {
+        need = wq::gemv_workspace_bytes(B, K, bits);
+    } else {
+        const bool single_group = group_size >= K;
+        if (single_group || group_size % 64 == 0) need = wq::tc_workspace_bytes(B, M, K, group_size, bits);
+    }
+    const size_t wide = wq::wide_workspace_bytes(B, M, K, group_size, bits);
+    return wide > need ? wide : need;
 }
 
 }  // extern "C"
@@ -253,7 +260,13 @@ int run_gemm(const float* x, int64_t B, int64_t K, const uint8_t* q, int64_t M, 
         }
         copies = false;
     };
-    if (wq::gemv_supported(p)) {
+    if (wq::wide_supported(p)) {
+        const size_t need = wq::wide_workspace_bytes(B, M, K, group_size, bits);
+        if (workspace_bytes < need || workspace == nullptr) return WQ_E_WORKSPACE;
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WQ_E_WORKSPACE;
+        fan_out();
+        e = wq::launch_wide(p, workspace, s);
+    } else if (wq::gemv_supported(p)) {
         const size_t need = wq::gemv_workspace_bytes(B, K, bits);
         if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return WQ_E_WORKSPACE;
         fan_out();

@@ -1,6 +1,7 @@
 // Internal launch interface between the C ABI (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -40,6 +41,20 @@ cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
 // these problems to it.
 bool gemv_imma_supported(const GemmProblem& p);
 cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
+
+// --- K1w: batches 3-32 on the integer tensor-core path ----------------------
+// int4 (groups a multiple of 64, or one group) and int8 (groups a multiple of
+// 64, or one group) codes with 16-byte aligned code rows: x' as three signed
+// base-256 digits per fold block, written by a prep kernel in the order the
+// MMA fragments read them; the weight is cut into units of 256 rows x one
+// fold block and every CTA takes an equal contiguous run of units
+// (stream-K), partial rows summed in a fixed order by the last CTA to arrive.
+// Workspace: the digit records, the partial rows, one counter per row block.
+constexpr int kWideMinBatch = 3;
+constexpr int kWideMaxBatch = 32;
+bool wide_supported(const GemmProblem& p);
+size_t wide_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits);
+cudaError_t launch_wide(const GemmProblem& p, void* workspace, cudaStream_t s);
 
 // --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
 // Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
@@ -110,6 +125,16 @@ cudaError_t launch_gptq_tail(double* work, int64_t rows, int64_t ld, int64_t c0,
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// cuTensorMapEncodeTiled from the driver (nullptr if unavailable), and a 2D
+// map over a row-major array: `inner` elements per row, `outer` rows,
+// `row_bytes` apart, boxes of box_inner x box_outer.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
 
 // Device address (current device) of the library's fault word: kernels OR in
 // 1 when a bounded pipeline mbarrier wait expires. nullptr if the symbol
