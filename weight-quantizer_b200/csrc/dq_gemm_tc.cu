@@ -49,6 +49,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -71,16 +72,53 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// A map is a pure function of its arguments, and a layer's weights are
+// encoded with the same arguments on every call: the last few encodings are
+// kept per host thread (no locking) and copied out on a repeat.
+namespace {
+struct MapKey {
+    const void* base;
+    uint64_t inner, outer, row_bytes;
+    uint32_t box_inner, box_outer;
+    int dt, swz;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && inner == o.inner && outer == o.outer && row_bytes == o.row_bytes &&
+               box_inner == o.box_inner && box_outer == o.box_outer && dt == o.dt && swz == o.swz;
+    }
+};
+constexpr int kMapCache = 16;
+struct MapCache {
+    MapKey key[kMapCache];
+    CUtensorMap map[kMapCache];
+    int used = 0, next = 0;
+};
+thread_local MapCache t_maps;
+}  // namespace
+
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    const MapKey k{base, inner, outer, row_bytes, box_inner, box_outer, (int)dt, (int)swz};
+    MapCache& c = t_maps;
+    for (int i = 0; i < c.used; ++i) {
+        if (c.key[i] == k) {
+            *map = c.map[i];
+            return true;
+        }
+    }
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    const int slot = c.used < kMapCache ? c.used++ : c.next;
+    if (slot == c.next) c.next = (c.next + 1) % kMapCache;
+    c.key[slot] = k;
+    c.map[slot] = *map;
+    return true;
 }
 
 
@@ -959,15 +997,27 @@ cudaError_t launch_bn_t(const GemmProblem& g, const TcWorkspace& w, cudaStream_t
     p.ldy = g.ldy;
     const size_t smem = (size_t)L::TOTAL + 1024;
     auto kern = dq_gemm_tc_kernel<BN, NS, BITS, SPLIT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Once per device: the shared-memory opt-in, and the register check. The
+    // setmaxnreg split assumes the launch gives every thread exactly
+    // LAUNCH_REGS registers; refuse to launch otherwise (the increase would
+    // wait for registers that do not exist).
+    constexpr int kDevs = 32;
+    static std::atomic<int> ready[kDevs];   // 0 not yet checked, 1 ready, 2 wrong register count
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    // the setmaxnreg split assumes the launch gives every thread exactly
-    // LAUNCH_REGS registers; refuse to launch otherwise (the increase would wait
-    // for registers that do not exist)
-    cudaFuncAttributes attr;
-    e = cudaFuncGetAttributes(&attr, kern);
-    if (e != cudaSuccess) return e;
-    if (attr.numRegs != Cfg<BN>::LAUNCH_REGS) return cudaErrorInvalidConfiguration;
+    const int known = (dev >= 0 && dev < kDevs) ? ready[dev].load(std::memory_order_relaxed) : 0;
+    if (known == 2) return cudaErrorInvalidConfiguration;
+    if (known == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cudaFuncAttributes attr;
+        e = cudaFuncGetAttributes(&attr, kern);
+        if (e != cudaSuccess) return e;
+        const bool ok = attr.numRegs == Cfg<BN>::LAUNCH_REGS;
+        if (dev >= 0 && dev < kDevs) ready[dev].store(ok ? 1 : 2, std::memory_order_relaxed);
+        if (!ok) return cudaErrorInvalidConfiguration;
+    }
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
     kern<<<dim3((unsigned)grid, (unsigned)p.splits), Cfg<BN>::THREADS, smem, s>>>(p, mq);

@@ -62,6 +62,7 @@
 // memory only, without multicast.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
@@ -70,12 +71,7 @@
 namespace wq {
 namespace {
 
-constexpr int kWideWarps = 8;                          // multiply warps
-constexpr int kWideThreads = (kWideWarps + 1) * 32;    // + one producer warp
-constexpr int kWideMmaThreads = kWideWarps * 32;
-constexpr int kWideMt = 2;                             // 16-row MMA tiles per multiply warp
-constexpr int kWideNg = 2;                             // batch tiles (of 8 rows) per accumulation pass
-constexpr int kWideRows = kWideWarps * kWideMt * 16;   // rows per row block: one TMA box
+constexpr int kWideRows = 256;                         // rows per row block: one TMA box
 constexpr int kWideLimbs = 3;                          // base-256 digits of a 23-bit signed integer
 constexpr int kWideMaxStages = 8;
 constexpr uint32_t kWideBias = 0x808080u;              // + 128 in each of the three digits
@@ -90,7 +86,7 @@ struct WideParams {
     float* y_extra[7];          // further outputs with y's layout (peer-mapped or local)
     int n_extra;
     float* y_all;               // NVLink-switch address reaching every rank's y, or nullptr
-    float* part;                // partial rows: [2 * grid][kWideMmaThreads][8 NT]
+    float* part;                // partial rows: [2 * grid][threads][E] (2048 NT floats per slot)
     int* counters;              // arrivals per row block (zeroed by the prep kernel)
     unsigned int* fault;
     int M, B, nfb, nrb, groups, fold_per_group, scale_rows;   // fold_per_group 0: one group
@@ -227,13 +223,29 @@ __global__ void __launch_bounds__(256) prep_digits_kernel(const float* x, const 
 }
 
 // ---- the dequant-GEMM -------------------------------------------------------
-template <int NT, int F, int BITS>
-__global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WideParams p,
-                                                                    const __grid_constant__ CUtensorMap mq,
-                                                                    const __grid_constant__ CUtensorMap ms,
-                                                                    const __grid_constant__ CUtensorMap mz) {
+// Warps: WARPS multiply warps of MT 16-row MMA tiles each (256 rows), then one
+// producer warp. With the producer's own warp every stage is refilled the
+// moment the last multiply warp releases it (at small batches the load
+// stream, not the multiply warps, sets the pace), and nine warps leave 168
+// registers a thread: batch tiles are accumulated in passes of NG.
+template <int NT, int MT>
+struct WideCfg {
+    static constexpr int WARPS = 16 / MT;
+    static constexpr int THREADS = WARPS * 32 + 32;   // + the producer warp
+    static constexpr int MMA_THREADS = WARPS * 32;
+    static constexpr int NG = NT < 2 ? NT : 2;        // batch tiles per accumulation pass
+    static constexpr int E = 4 * MT * NT;             // fp32 accumulators per thread
+    static_assert(WARPS * MT * 16 == kWideRows, "a row block is one TMA box of rows");
+};
+
+template <int NT, int F, int BITS, int MT>
+__global__ void __launch_bounds__(WideCfg<NT, MT>::THREADS, 1)
+    gemv_wide_kernel(const WideParams p, const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap ms,
+                     const __grid_constant__ CUtensorMap mz) {
     using S = WideShape<F, BITS>;
-    constexpr int E = 8 * NT;   // accumulators per thread: 2 row tiles x 2 rows x NT tiles x 2 columns
+    using C = WideCfg<NT, MT>;
+    constexpr int E = C::E;
+    constexpr int NG = C::NG;
     extern __shared__ unsigned char smem_raw[];
     // stages start on a 1024-byte boundary (TMA destinations need 128)
     const uint32_t raw = smem_addr(smem_raw);
@@ -248,10 +260,10 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t P = gridDim.x, cta = blockIdx.x;
     const int64_t u0 = unit_start(cta, p.units, P), u1 = unit_start(cta + 1, p.units, P);
-    if (warp == kWideWarps && lane == 0) {
+    if (warp == C::WARPS && lane == 0) {
         for (int s = 0; s < p.ns; ++s) {
             mbar_init(full0 + 8u * (uint32_t)s, 1);
-            mbar_init(cons0 + 8u * (uint32_t)s, (uint32_t)kWideWarps);
+            mbar_init(cons0 + 8u * (uint32_t)s, (uint32_t)C::WARPS);
         }
         fence_mbarrier_init();
     }
@@ -259,8 +271,8 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
     // the prep kernel's records and counters
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    if (warp == kWideWarps) {
-        // ---- producer: one code box and one record per unit ------------------
+    if (warp == C::WARPS) {
+        // ---- producer warp: one code box, two table boxes and one record per unit
         if (lane == 0) {
             bool faulted = false;
             uint32_t filled = 0, fill_par = 0;
@@ -309,18 +321,17 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
     }
 
     // ---- multiply warps ---------------------------------------------------------
-    // The work of a warp is a sequence of steps, one per (unit, batch tile of 8
-    // rows). A step issues its MMAs into one of two integer accumulator sets
-    // and then folds the previous step's set, whose MMAs have had a whole step
-    // to complete, so the fold's conversions and multiply-adds overlap the
-    // tensor pipe instead of waiting for it. Per unit (first step) come the
-    // stage wait and this thread's code words; scales and zeros are read after
-    // the previous unit's last fold, which still needs the old ones. Units go
-    // in pairs so that which accumulator set a step uses is known at compile
-    // time.
+    // The CTA's run of units is walked one row-block segment at a time: the
+    // units of a segment, then the segment's output. Per unit a warp waits for
+    // the stage, loads its code words, runs the MMAs of every batch tile (in
+    // passes of NG tiles, each folded into the fp32 accumulators right
+    // after its MMAs) and releases the stage. With one batch tile (up to 8
+    // batch rows) a unit is short, so two units are taken per iteration: their
+    // loads, MMAs and folds interleave, which hides the shared-memory and
+    // barrier latencies of one behind the work of the other.
     const int g = lane >> 2;   // MMA group: rows g and g + 8, B column g
     const int t = lane & 3;    // thread in group: C columns 2t and 2t + 1
-    const int wrow = warp * (kWideMt * 16);
+    const int wrow = warp * (MT * 16);   // this warp's first row in the row block
     float acc[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) acc[i] = 0.0f;
@@ -329,7 +340,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
     // y (+ bias) into every output of rows blk*256 + this thread's rows
     auto write_out = [&](int blk, const float (&val)[E]) {
 #pragma unroll
-        for (int mt = 0; mt < kWideMt; ++mt) {
+        for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
                 const int row = blk * kWideRows + wrow + mt * 16 + g + 8 * rr;
@@ -366,18 +377,18 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
         } else {
             // slot 1 when the CTA's run started in an earlier row block, else 0
             const int which = u0 < ub ? 1 : 0;
-            float* dst = p.part + ((size_t)(2 * cta + which) * kWideMmaThreads + threadIdx.x) * E;
+            float* dst = p.part + ((size_t)(2 * cta + which) * C::MMA_THREADS + threadIdx.x) * E;
 #pragma unroll
             for (int i = 0; i < E; i += 4)
                 __stcg(reinterpret_cast<float4*>(dst + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
             __threadfence();
-            named_barrier(1, kWideMmaThreads);
+            named_barrier(1, C::MMA_THREADS);
             const int64_t cf = unit_owner(ub, p.units, P), cl = unit_owner(ue - 1, p.units, P);
             if (threadIdx.x == 0) {
                 const int old = atomicAdd(p.counters + blk, 1);
                 *flag = old == (int)(cl - cf) ? 1 : 0;
             }
-            named_barrier(1, kWideMmaThreads);
+            named_barrier(1, C::MMA_THREADS);
             if (*flag) {
                 __threadfence();
                 float sum[E];
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
                 for (int i = 0; i < E; ++i) sum[i] = 0.0f;
                 for (int64_t c = cf; c <= cl; ++c) {
                     const int wh = unit_start(c, p.units, P) < ub ? 1 : 0;
-                    const float* src = p.part + ((size_t)(2 * c + wh) * kWideMmaThreads + threadIdx.x) * E;
+                    const float* src = p.part + ((size_t)(2 * c + wh) * C::MMA_THREADS + threadIdx.x) * E;
 #pragma unroll
                     for (int i = 0; i < E; i += 4) {
                         const float4 q = __ldcg(reinterpret_cast<const float4*>(src + i));
@@ -402,89 +413,37 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
         for (int i = 0; i < E; ++i) acc[i] = 0.0f;
     };
 
-    using Acc = int[kWideMt][kWideLimbs][4];
-    // fold of one step's integer accumulators (batch tile J) into acc
-    auto fold = [&](const Acc& c, const int J, const float4 f, const float (&sc_)[kWideMt][2],
-                    const float (&zr_)[kWideMt][2]) {
-#pragma unroll
-        for (int mt = 0; mt < kWideMt; ++mt) {
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int i = 2 * rr + cc;
-                    const int c01 = c[mt][0][i] + 256 * c[mt][1][i];   // exact in s32
-                    float v = fmaf((float)c[mt][2][i], 65536.0f, (float)c01);
-                    const float pw = cc ? f.z : f.x;
-                    const float sx = cc ? f.w : f.y;
-                    v = fmaf(-zr_[mt][rr], sx, v);
-                    float& a = acc[((mt * 2 + rr) * NT + J) * 2 + cc];
-                    a = fmaf(sc_[mt][rr] * pw, v, a);
-                }
-            }
-        }
-    };
+    using Words = uint32_t[MT][2][S::WPT];
+    using Tab = float[MT][2];
+    using Acc = int[MT][kWideLimbs][NG][4];
 
-    // state of the unit being read
+    // stage ring position of the next unit
     int s = 0;
     uint32_t par = 0;
-    int rb = (int)(u0 / p.nfb), fb = (int)(u0 % p.nfb);
-    int64_t seg0 = u0;
-    uint32_t aw[kWideMt][2][S::WPT];
-    float sc[kWideMt][2], zr[kWideMt][2];   // of the unit whose steps are being folded
-    float4 fbt = make_float4(0.f, 0.f, 0.f, 0.f);   // fold factors of the previous step
-    const unsigned char* stg = stages;
-    // the previous step
-    bool pvalid = false, pflush = false;
-    int prb = 0;
-    int64_t pseg0 = 0, pu = 0;
-    Acc cA, cB;
-
-    // scales and zeros of unit (blk, f) for this thread's rows
-    auto load_tables = [&](int blk, int f) {
-        const int gi = p.fold_per_group > 0 ? f / p.fold_per_group : 0;
-        if (p.tab_box) {
-            // rows past M are zero-filled by the copy
-            const float* ts = reinterpret_cast<const float*>(stg + p.tab_off);
-            const float* tz = ts + kWideRows * kWideTabGroups;
-            const int gc = gi & (kWideTabGroups - 1);
-#pragma unroll
-            for (int mt = 0; mt < kWideMt; ++mt) {
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const int r = wrow + mt * 16 + g + 8 * rr;
-                    sc[mt][rr] = ts[r * kWideTabGroups + gc];
-                    zr[mt][rr] = tz[r * kWideTabGroups + gc];
-                }
-            }
-        } else {
-#pragma unroll
-            for (int mt = 0; mt < kWideMt; ++mt) {
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const int row = blk * kWideRows + wrow + mt * 16 + g + 8 * rr;
-                    sc[mt][rr] = zr[mt][rr] = 0.0f;
-                    if (row < p.M) {
-                        const int64_t idx = p.scale_rows == 1 ? (int64_t)gi : (int64_t)row * p.groups + gi;
-                        sc[mt][rr] = __ldg(p.scales + idx);
-                        zr[mt][rr] = __ldg(p.zeros + idx);
-                    }
-                }
-            }
+    auto next_stage = [&](int& st, uint32_t& pr) {
+        st = s;
+        pr = par;
+        if (++s == p.ns) {
+            s = 0;
+            par ^= 1u;
         }
     };
-
-    // all steps of unit u; X / Y: the accumulator sets of its even / odd steps
-    auto unit_steps = [&](int64_t u, Acc& X, Acc& Y) {
-        if (!faulted && !mbar_wait_bounded(full0 + 8u * (uint32_t)s, par)) {
+    auto stage_wait = [&](int st, uint32_t pr) {
+        if (!faulted && !mbar_wait_bounded(full0 + 8u * (uint32_t)st, pr)) {
             faulted = true;
             atomicOr(p.fault, 1u);
         }
-        stg = stages + (size_t)s * p.stage_bytes;
-        const unsigned char* rec = stg + S::CODE_BYTES;
-        // this thread's code words of rows g, g + 8 of both row tiles
+    };
+    auto release = [&](int st) {
+        // mbarrier.arrive releases: this warp's shared-memory reads of the
+        // stage, all earlier in program order, are ordered before the refill
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cons0 + 8u * (uint32_t)st);
+    };
+    // this thread's code words of rows g, g + 8 of both row tiles
+    auto load_codes = [&](const unsigned char* stg, Words& aw) {
 #pragma unroll
-        for (int mt = 0; mt < kWideMt; ++mt) {
+        for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
                 const unsigned char* src = stg + (size_t)(wrow + mt * 16 + g + 8 * rr) * S::RB + t * (S::RB / 4);
@@ -501,127 +460,201 @@ __global__ void __launch_bounds__(kWideThreads, 1) gemv_wide_kernel(const WidePa
                 }
             }
         }
-        uint32_t dep = 0;   // every value read from the stage, so the release follows the reads
-        // A segment ended with the previous unit: fold its last step and write
-        // the segment out before this unit's MMAs are issued (at most twice per
-        // CTA), so nothing else is in flight meanwhile.
-        // (the previous unit's last step is in Y whatever the parity of NT)
-        const bool early = pflush;
-        if (early) {
-            fold(Y, NT - 1, fbt, sc, zr);
-            flush(prb, pseg0, pu);
+    };
+    // scales and zeros of unit (blk, f), this thread's rows: from global memory
+    // (issued before the stage wait), or from the stage's table boxes
+    auto tables_global = [&](int blk, int f, Tab& sc, Tab& zr) {
+        const int gi = p.fold_per_group > 0 ? f / p.fold_per_group : 0;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int row = blk * kWideRows + wrow + mt * 16 + g + 8 * rr;
+                sc[mt][rr] = zr[mt][rr] = 0.0f;
+                if (row < p.M) {
+                    const int64_t idx = p.scale_rows == 1 ? (int64_t)gi : (int64_t)row * p.groups + gi;
+                    sc[mt][rr] = __ldg(p.scales + idx);
+                    zr[mt][rr] = __ldg(p.zeros + idx);
+                }
+            }
         }
+    };
+    auto tables_stage = [&](const unsigned char* stg, int f, Tab& sc, Tab& zr) {
+        const int gi = p.fold_per_group > 0 ? f / p.fold_per_group : 0;
+        const float* ts = reinterpret_cast<const float*>(stg + p.tab_off);   // rows past M are zero-filled
+        const float* tz = ts + kWideRows * kWideTabGroups;
+        const int gc = gi & (kWideTabGroups - 1);
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            Acc& cur = (j & 1) ? Y : X;
-            Acc& prv = (j & 1) ? X : Y;
+        for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-            for (int mt = 0; mt < kWideMt; ++mt)
+            for (int rr = 0; rr < 2; ++rr) {
+                const int r = wrow + mt * 16 + g + 8 * rr;
+                sc[mt][rr] = ts[r * kWideTabGroups + gc];
+                zr[mt][rr] = tz[r * kWideTabGroups + gc];
+            }
+        }
+    };
+    // the MMAs of batch tiles ng0 .. ng0 + NG - 1 of one unit
+    auto mma_pass = [&](const unsigned char* rec, const Words& aw, const int ng0, Acc& c) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int l = 0; l < kWideLimbs; ++l)
+#pragma unroll
+                for (int j = 0; j < NG; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) c[mt][l][j][i] = 0;
+#pragma unroll
+        for (int h = 0; h < S::H; ++h) {
+            // A fragments of k-steps 2h and 2h + 1
+            uint32_t af[MT][2][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+                for (int ss = 0; ss < 2; ++ss) {
+                    const int ks = 2 * h + ss;
+                    if constexpr (BITS == 4) {
+                        af[mt][ss][0] = aw[mt][0][ks] & 0x0F0F0F0Fu;
+                        af[mt][ss][1] = aw[mt][1][ks] & 0x0F0F0F0Fu;
+                        af[mt][ss][2] = (aw[mt][0][ks] >> 4) & 0x0F0F0F0Fu;
+                        af[mt][ss][3] = (aw[mt][1][ks] >> 4) & 0x0F0F0F0Fu;
+                    } else {
+                        af[mt][ss][0] = aw[mt][0][2 * ks];
+                        af[mt][ss][1] = aw[mt][1][2 * ks];
+                        af[mt][ss][2] = aw[mt][0][2 * ks + 1];
+                        af[mt][ss][3] = aw[mt][1][2 * ks + 1];
+                    }
+                }
+            }
+            // B fragments of both k-steps for every digit and batch tile
+            uint4 bq[kWideLimbs][NG];
+#pragma unroll
+            for (int l = 0; l < kWideLimbs; ++l)
+#pragma unroll
+                for (int j = 0; j < NG; ++j)
+                    if (ng0 + j < NT)
+                        bq[l][j] = *reinterpret_cast<const uint4*>(
+                            rec + (size_t)((l * NT + ng0 + j) * S::H + h) * kWidePiece + (size_t)lane * 16);
+            // k-step outermost: consecutive MMAs write different accumulators
+#pragma unroll
+            for (int ss = 0; ss < 2; ++ss)
 #pragma unroll
                 for (int l = 0; l < kWideLimbs; ++l)
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) cur[mt][l][i] = 0;
+                    for (int j = 0; j < NG; ++j) {
+                        if (ng0 + j >= NT) continue;
 #pragma unroll
-            for (int h = 0; h < S::H; ++h) {
-                // A fragments of k-steps 2h and 2h + 1
-                uint32_t af[kWideMt][2][4];
+                        for (int mt = 0; mt < MT; ++mt)
+                            mma_u8s8(c[mt][l][j], af[mt][ss][0], af[mt][ss][1], af[mt][ss][2], af[mt][ss][3],
+                                     ss ? bq[l][j].z : bq[l][j].x, ss ? bq[l][j].w : bq[l][j].y);
+                    }
+        }
+    };
+    // fold factors of this lane's batch columns 8 ng + 2t, 8 ng + 2t + 1
+    auto load_fbt = [&](const unsigned char* rec, const int ng0, float4 (&f)[NG]) {
 #pragma unroll
-                for (int mt = 0; mt < kWideMt; ++mt) {
+        for (int j = 0; j < NG; ++j)
+            if (ng0 + j < NT)
+                f[j] = *reinterpret_cast<const float4*>(rec + S::dig_bytes(NT) + (size_t)(8 * (ng0 + j) + 2 * t) * 8);
+    };
+    // fold: C[m, n] of digit l, row g or g + 8 (rr), batch column 2t + cc
+    auto fold = [&](const Acc& c, const int ng0, const float4 (&f)[NG], const Tab& sc, const Tab& zr) {
 #pragma unroll
-                    for (int ss = 0; ss < 2; ++ss) {
-                        const int ks = 2 * h + ss;
-                        if constexpr (BITS == 4) {
-                            af[mt][ss][0] = aw[mt][0][ks] & 0x0F0F0F0Fu;
-                            af[mt][ss][1] = aw[mt][1][ks] & 0x0F0F0F0Fu;
-                            af[mt][ss][2] = (aw[mt][0][ks] >> 4) & 0x0F0F0F0Fu;
-                            af[mt][ss][3] = (aw[mt][1][ks] >> 4) & 0x0F0F0F0Fu;
-                        } else {
-                            af[mt][ss][0] = aw[mt][0][2 * ks];
-                            af[mt][ss][1] = aw[mt][1][2 * ks];
-                            af[mt][ss][2] = aw[mt][0][2 * ks + 1];
-                            af[mt][ss][3] = aw[mt][1][2 * ks + 1];
-                        }
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+#pragma unroll
+                for (int j = 0; j < NG; ++j) {
+                    if (ng0 + j >= NT) continue;
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        const int i = 2 * rr + cc;
+                        const int c01 = c[mt][0][j][i] + 256 * c[mt][1][j][i];   // exact in s32
+                        float v = fmaf((float)c[mt][2][j][i], 65536.0f, (float)c01);
+                        const float pw = cc ? f[j].z : f[j].x;
+                        const float sx = cc ? f[j].w : f[j].y;
+                        v = fmaf(-zr[mt][rr], sx, v);
+                        float& a = acc[((mt * 2 + rr) * NT + ng0 + j) * 2 + cc];
+                        a = fmaf(sc[mt][rr] * pw, v, a);
                     }
                 }
-                // B fragments of both k-steps, every digit
-                uint4 bq[kWideLimbs];
-#pragma unroll
-                for (int l = 0; l < kWideLimbs; ++l) {
-                    bq[l] = *reinterpret_cast<const uint4*>(rec + (size_t)((l * NT + j) * S::H + h) * kWidePiece +
-                                                            (size_t)lane * 16);
-                    dep ^= bq[l].x ^ bq[l].y ^ bq[l].z ^ bq[l].w;
-                }
-                // k-step outermost: consecutive MMAs write different accumulators
-#pragma unroll
-                for (int ss = 0; ss < 2; ++ss)
-#pragma unroll
-                    for (int l = 0; l < kWideLimbs; ++l)
-#pragma unroll
-                        for (int mt = 0; mt < kWideMt; ++mt)
-                            mma_u8s8(cur[mt][l], af[mt][ss][0], af[mt][ss][1], af[mt][ss][2], af[mt][ss][3],
-                                     ss ? bq[l].z : bq[l].x, ss ? bq[l].w : bq[l].y);
             }
-            // fold the previous step while these MMAs run
-            if (j == 0) {
-                if (pvalid && !early) fold(prv, NT - 1, fbt, sc, zr);
-                load_tables(rb, fb);
-            } else {
-                fold(prv, j - 1, fbt, sc, zr);
-            }
-            fbt = *reinterpret_cast<const float4*>(rec + S::dig_bytes(NT) + (size_t)(8 * j + 2 * t) * 8);
-            if (j == NT - 1) {
-                // release the stage once every value read from it is in registers
-                dep ^= __float_as_uint(fbt.x) ^ __float_as_uint(fbt.y) ^ __float_as_uint(fbt.z) ^
-                       __float_as_uint(fbt.w);
-#pragma unroll
-                for (int mt = 0; mt < kWideMt; ++mt)
-#pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        dep ^= __float_as_uint(sc[mt][rr]) ^ __float_as_uint(zr[mt][rr]);
-#pragma unroll
-                        for (int w = 0; w < S::WPT; ++w) dep ^= aw[mt][rr][w];
-                    }
-                __syncwarp();
-                if (lane == 0)
-                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n\t// %1" ::"r"(cons0 + 8u * (uint32_t)s),
-                                 "r"(dep)
-                                 : "memory");
-            }
-        }
-        pvalid = true;
-        pflush = fb == p.nfb - 1 || u == u1 - 1;
-        prb = rb;
-        pseg0 = seg0;
-        pu = u;
-        if (pflush) seg0 = u + 1;
-        if (++fb == p.nfb) {
-            fb = 0;
-            ++rb;
-        }
-        if (++s == p.ns) {
-            s = 0;
-            par ^= 1u;
         }
     };
 
-#pragma unroll 1
-    for (int64_t u = u0; u < u1; u += 2) {
-        unit_steps(u, cA, cB);
-        // a unit of an odd number of steps leaves the next one starting on the other set
-        if (u + 1 < u1) {
-            if constexpr (NT & 1)
-                unit_steps(u + 1, cB, cA);
-            else
-                unit_steps(u + 1, cA, cB);
+    // one unit (row block blk, fold block f)
+    auto one_unit = [&](int blk, int f) {
+        int st;
+        uint32_t pr;
+        next_stage(st, pr);
+        Tab sc, zr;
+        if (!p.tab_box) tables_global(blk, f, sc, zr);
+        stage_wait(st, pr);
+        const unsigned char* stg = stages + (size_t)st * p.stage_bytes;
+        const unsigned char* rec = stg + S::CODE_BYTES;
+        Words aw;
+        load_codes(stg, aw);
+        if (p.tab_box) tables_stage(stg, f, sc, zr);
+#pragma unroll
+        for (int ng0 = 0; ng0 < NT; ng0 += NG) {
+            Acc c;
+            mma_pass(rec, aw, ng0, c);
+            float4 fbt[NG];
+            load_fbt(rec, ng0, fbt);
+            if (ng0 + NG >= NT) release(st);
+            fold(c, ng0, fbt, sc, zr);
         }
+    };
+    // two consecutive units of one row block (one batch tile only)
+    auto two_units = [&](int blk, int f) {
+        int st0, st1;
+        uint32_t pr0, pr1;
+        next_stage(st0, pr0);
+        next_stage(st1, pr1);
+        Tab sc0, zr0, sc1, zr1;
+        if (!p.tab_box) {
+            tables_global(blk, f, sc0, zr0);
+            tables_global(blk, f + 1, sc1, zr1);
+        }
+        stage_wait(st0, pr0);
+        stage_wait(st1, pr1);
+        const unsigned char* stg0 = stages + (size_t)st0 * p.stage_bytes;
+        const unsigned char* stg1 = stages + (size_t)st1 * p.stage_bytes;
+        Words aw0, aw1;
+        load_codes(stg0, aw0);
+        load_codes(stg1, aw1);
+        if (p.tab_box) {
+            tables_stage(stg0, f, sc0, zr0);
+            tables_stage(stg1, f + 1, sc1, zr1);
+        }
+        Acc c0, c1;
+        mma_pass(stg0 + S::CODE_BYTES, aw0, 0, c0);
+        mma_pass(stg1 + S::CODE_BYTES, aw1, 0, c1);
+        float4 f0[NG], f1[NG];
+        load_fbt(stg0 + S::CODE_BYTES, 0, f0);
+        load_fbt(stg1 + S::CODE_BYTES, 0, f1);
+        release(st0);
+        release(st1);
+        fold(c0, 0, f0, sc0, zr0);   // in unit order, as one_unit would
+        fold(c1, 0, f1, sc1, zr1);
+    };
+
+    int64_t u = u0;
+#pragma unroll 1
+    while (u < u1) {
+        const int blk = (int)(u / p.nfb);
+        const int64_t seg_first = u;
+        const int64_t row_end = (int64_t)(blk + 1) * p.nfb;
+        const int64_t seg_end = u1 < row_end ? u1 : row_end;
+        int f = (int)(u - (int64_t)blk * p.nfb);
+        if constexpr (NT == 1) {
+#pragma unroll 1
+            for (; u + 1 < seg_end; u += 2, f += 2) two_units(blk, f);
+        }
+#pragma unroll 1
+        for (; u < seg_end; ++u, ++f) one_unit(blk, f);
+        flush(blk, seg_first, seg_end - 1);
     }
-    // the last step: its set follows from the number of steps
-    const bool last_in_b = ((u1 - u0) * NT - 1) & 1;
-    if (last_in_b)
-        fold(cB, NT - 1, fbt, sc, zr);
-    else
-        fold(cA, NT - 1, fbt, sc, zr);
-    flush(prb, pseg0, pu);
 }
 
 // ---- host side ------------------------------------------------------------------
@@ -685,7 +718,7 @@ struct WideWorkspace {
 
 size_t wide_bytes(const WidePlan& pl) {
     return (size_t)(round256((int64_t)pl.nfb * pl.rec_bytes) +
-                    round256((int64_t)2 * pl.grid * kWideMmaThreads * 8 * pl.NT * 4) + round256((int64_t)pl.nrb * 4));
+                    round256((int64_t)2 * pl.grid * kWideRows * 8 * pl.NT * 4) + round256((int64_t)pl.nrb * 4));
 }
 
 WideWorkspace wide_carve(void* ws, const WidePlan& pl) {
@@ -694,7 +727,7 @@ WideWorkspace wide_carve(void* ws, const WidePlan& pl) {
     w.rec = q;
     q += round256((int64_t)pl.nfb * pl.rec_bytes);
     w.part = reinterpret_cast<float*>(q);
-    q += round256((int64_t)2 * pl.grid * kWideMmaThreads * 8 * pl.NT * 4);
+    q += round256((int64_t)2 * pl.grid * kWideRows * 8 * pl.NT * 4);
     w.counters = reinterpret_cast<int*>(q);
     return w;
 }
@@ -726,11 +759,21 @@ struct WideMaps {
 
 template <int NT, int F, int BITS>
 cudaError_t launch_main(const WideParams& p, const WideMaps& m, const WidePlan& pl, cudaStream_t s) {
-    auto kern = gemv_wide_kernel<NT, F, BITS>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    constexpr int MT = 2;   // 8 multiply warps of two row tiles
+    auto kern = gemv_wide_kernel<NT, F, BITS, MT>;
+    // the shared-memory opt-in is set once per device and size (the last size is kept)
+    constexpr int kDevs = 32;
+    static std::atomic<size_t> opted[kDevs];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kDevs || opted[dev].load(std::memory_order_relaxed) != pl.smem) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < kDevs) opted[dev].store(pl.smem, std::memory_order_relaxed);
+    }
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)pl.grid), dim3(kWideThreads), pl.smem, s, attr);
+    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)pl.grid), dim3(WideCfg<NT, MT>::THREADS), pl.smem, s, attr);
     return cudaLaunchKernelEx(&cfg, kern, p, m.q, m.s, m.z);
 }
 
@@ -749,7 +792,14 @@ cudaError_t launch_fb(const GemmProblem& g, const WidePlan& pl, const WideWorksp
 
 }  // namespace
 
+// Above 16 batch rows this kernel is bound by its MMA count (3 digits x
+// ceil(B / 8) tiles); there the tcgen05 kernel with split-K is faster on
+// small layers (measured: 4096 x 4095 at batch 32, 47 us here against 37 us),
+// and this one on large ones (28672 x 8192 at batch 32: 104 us against 136).
+constexpr int64_t kWideMinCodesAbove16 = (int64_t)1 << 25;
+
 bool wide_supported(const GemmProblem& g) {
+    if (g.B > 16 && g.M * g.K < kWideMinCodesAbove16) return false;
     WidePlan pl;
     if (!wide_plan(g.B, g.M, g.K, g.group_size, g.bits, false, pl)) return false;
     if (g.groups > 1 && g.group_size % pl.F != 0) return false;
