@@ -27,6 +27,7 @@ struct GemmProblem {
 };
 
 // --- K1: streaming decode kernel (small batch, weight-stream bound) --------
+// Batches up to 4; the C ABI sends batches 3-4 to K1w first when it applies.
 constexpr int kGemvMaxBatch = 4;
 // Workspace the decode path needs for this problem (0 if it does not apply).
 size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
@@ -34,11 +35,11 @@ size_t gemv_workspace_bytes(int64_t B, int64_t K, int bits);
 // batch, shared-memory fit).
 bool gemv_supported(const GemmProblem& p);
 cudaError_t launch_gemv(const GemmProblem& p, void* workspace, cudaStream_t s);
-// int4 codes at batches 1-4 on the integer tensor-core path (mma.sync
+// int4 codes at batches 1-2 on the integer tensor-core path (mma.sync
 // m16n8k32 u8 x s8: codes widened to bytes, x' as three signed base-256
-// digits; batches 3-4 as two launches), when groups are multiples of 64 (or
-// one group), K <= 8192 and the tables can be bulk-copied; launch_gemv routes
-// these problems to it.
+// digits), when groups are multiples of 64 (or one group), K <= 8192 and the
+// tables can be bulk-copied; launch_gemv routes these problems to it, and
+// batches 3-4 that K1w does not take as two launches.
 bool gemv_imma_supported(const GemmProblem& p);
 cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
 
@@ -49,6 +50,8 @@ cudaError_t launch_gemv_imma(const GemmProblem& p, cudaStream_t s);
 // MMA fragments read them; the weight is cut into units of 256 rows x one
 // fold block and every CTA takes an equal contiguous run of units
 // (stream-K), partial rows summed in a fixed order by the last CTA to arrive.
+// Above 16 batch rows it takes only layers of at least 2^25 codes (smaller
+// ones run faster on the tcgen05 kernel with split-K).
 // Workspace: the digit records, the partial rows, one counter per row block.
 constexpr int kWideMinBatch = 3;
 constexpr int kWideMaxBatch = 32;
@@ -56,7 +59,7 @@ bool wide_supported(const GemmProblem& p);
 size_t wide_workspace_bytes(int64_t B, int64_t M, int64_t K, int group_size, int bits);
 cudaError_t launch_wide(const GemmProblem& p, void* workspace, cudaStream_t s);
 
-// --- K2: tcgen05/TMEM tensor-core kernel (batch >= 5) -----------------------
+// --- K2: tcgen05/TMEM tensor-core kernel (batches above 32, and 5-32 where K1w does not run)
 // Applies when rows are 16-byte aligned and groups are multiples of 64 (or a
 // single group). Workspace: the fp16 hi/lo planes of x', 1/S_b, the
 // per-group sums of x' (for zero points that are not integers) and, when
