@@ -80,6 +80,20 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// L2 policy that keeps lines past ordinary ones (evict_last) for all of a
+// copy's bytes, and the bulk copy above with that policy as its L2 hint.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_copy_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                                   uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
 // Orders this thread's generic-proxy shared-memory accesses (and those it has
 // observed) before later async-proxy accesses (TMA, bulk copies, tcgen05) to
 // the same shared memory, and the reverse.

@@ -126,7 +126,11 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int kBand = 16;        // batch tiles per rasterization band
+// Output tiles are ordered in bands of batch tiles (weight tiles inside a
+// band): the x' planes of one band (KT * 256 * BN bytes per batch tile) are
+// kept under this size so that they stay in L2 while the weights stream past
+// once per band.
+constexpr int64_t kBandBytes = (int64_t)40 << 20;
 // warpgroup 0: producers, MMA issuer, scheduler; then the dequant warpgroups;
 // the last warpgroup runs the epilogue
 constexpr int kWarpB = 0, kWarpMma = 1, kWarpCodes = 2, kWarpSched = 3, kWarpDq0 = 4;
@@ -193,6 +197,7 @@ struct TcParams {
     unsigned int* fault;
     int M, B, KT, groups, ktg, ngroups, scale_rows;
     int tiles_m, tiles_n;
+    int band;             // batch tiles per rasterization band
     int64_t ldy;
 };
 
@@ -329,12 +334,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     auto stage_b = [&](int s) { return sbase + (uint32_t)(s * L::STAGE); };
     auto stage_c = [&](int c) { return sbase + (uint32_t)(L::C_OFF + c * L::C_STAGE); };
 
-    // tile coordinates (bands of kBand batch tiles, weight tiles inside a band)
-    const int band = blockIdx.x / (p.tiles_m * kBand);
-    const int inner = blockIdx.x - band * p.tiles_m * kBand;
-    const int bw = min(kBand, p.tiles_n - band * kBand);
+    // tile coordinates (bands of p.band batch tiles, weight tiles inside a band)
+    const int band = blockIdx.x / (p.tiles_m * p.band);
+    const int inner = blockIdx.x - band * p.tiles_m * p.band;
+    const int bw = min(p.band, p.tiles_n - band * p.band);
     const int m_tile = inner / bw;
-    const int n_tile = band * kBand + (inner - m_tile * bw);
+    const int n_tile = band * p.band + (inner - m_tile * bw);
     const int m0 = m_tile * BM, n0 = n_tile * BN;
     // split-K: this CTA's K tiles [t0, t0 + KTL) and groups [g0, g0 + NGL);
     // split boundaries fall on group and code-box boundaries (p.gran tiles)
@@ -418,8 +423,12 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     if (warp < kWarpDq0) {
       set_regs<C::REGS_CTL, C::LAUNCH_REGS>();
       if (warp == kWarpB) {
-        // x' planes: one bulk copy of both planes of a K tile per stage
+        // x' planes: one bulk copy of both planes of a K tile per stage. The
+        // planes of a band are read by every weight tile of the band, the codes
+        // by the band's few concurrent CTAs: the planes are marked to stay in
+        // L2 past the code stream.
         if (lane == 0) {
+            const uint64_t keep = l2_policy_evict_last();
             const uint32_t tile_bytes = (uint32_t)L::STAGE;
             const unsigned char* src = p.planes + ((size_t)n_tile * p.KT + T0()) * tile_bytes;
             int s = 0;
@@ -427,7 +436,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             for (int t = 0; t < KTL(); ++t) {
                 if (t >= NS) wait(empty_b(s), ph ^ 1u);
                 mbar_arrive_expect_tx(full_b(s), tile_bytes);
-                bulk_copy_g2s(stage_b(s), src, tile_bytes, full_b(s));
+                bulk_copy_g2s_hint(stage_b(s), src, tile_bytes, full_b(s), keep);
                 src += tile_bytes;
                 if (++s == NS) {
                     s = 0;
@@ -994,6 +1003,14 @@ cudaError_t launch_bn_t(const GemmProblem& g, const TcWorkspace& w, cudaStream_t
     p.scale_rows = g.scale_rows;
     p.tiles_m = (int)((g.M + BM - 1) / BM);
     p.tiles_n = (int)((g.B + BN - 1) / BN);
+    {
+        // the fewest bands whose x' fits kBandBytes, then equal band widths
+        const int64_t per_tile = (int64_t)p.KT * 256 * BN;
+        int64_t most = kBandBytes / per_tile;
+        if (most < 1) most = 1;
+        const int64_t bands = (p.tiles_n + most - 1) / most;
+        p.band = (int)((p.tiles_n + bands - 1) / bands);
+    }
     p.ldy = g.ldy;
     const size_t smem = (size_t)L::TOTAL + 1024;
     auto kern = dq_gemm_tc_kernel<BN, NS, BITS, SPLIT>;
