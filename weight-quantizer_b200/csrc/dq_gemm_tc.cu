@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_addr(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     auto bar = [&](int i) -> uint32_t { return sbase + L::BAR_OFF + 8u * (uint32_t)i; };
     auto full_b = [&](int s) { return bar(s); };
     auto empty_b = [&](int s) { return bar(NS + s); };
@@ -388,6 +389,10 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Launched with programmatic stream serialization: the setup above
+    // overlaps the prep kernel's tail; nothing below reads global memory
+    // before that kernel (and every earlier one on the stream) has completed.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::TMEM_SLOT);
     const uint32_t tmem_a0 = tmem + (uint32_t)(2 * C::ACCW);
     bool faulted = false;
@@ -825,6 +830,10 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const float* x, const float
                                                      int gsz, int ngroups, int bpad, float* xsum, int* counters,
                                                      int ncounters) {
     __shared__ float red[8];
+    // x may be the previous kernel's output; the tensor-core kernel that
+    // follows waits for this one to complete before it reads the planes
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int b = blockIdx.x;
     if (b == 0)   // split-K arrival counters of the tensor-core kernel that follows
         for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
@@ -1037,8 +1046,17 @@ cudaError_t launch_bn_t(const GemmProblem& g, const TcWorkspace& w, cudaStream_t
     }
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    kern<<<dim3((unsigned)grid, (unsigned)p.splits), Cfg<BN>::THREADS, smem, s>>>(p, mq);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, (unsigned)p.splits);
+    cfg.blockDim = dim3(Cfg<BN>::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p, mq);
 }
 
 // the split-K epilogue is a separate instantiation, so the unsplit kernel
@@ -1076,10 +1094,18 @@ cudaError_t launch_tc(const GemmProblem& g, void* workspace, cudaStream_t s) {
     const int64_t bpad = bpad_of(g.B);
     const int64_t ng = ngroups_of(g.K, g.group_size);
     const int gsz = ng == 1 ? (int)g.K : g.group_size;
-    prep_x_kernel<<<(unsigned)bpad, 256, 0, s>>>(g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn,
-                                                 g.bits == 4, w.planes, w.inv_s, gsz, (int)ng, (int)bpad, w.xsum,
-                                                 w.counters, w.plan.splits > 1 ? (int)w.tiles : 0);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)bpad);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, prep_x_kernel, g.x, g.channel, (int)g.B, (int)g.K, (int)kt_of(g.K), bn,
+                                       g.bits == 4, w.planes, w.inv_s, gsz, (int)ng, (int)bpad, w.xsum, w.counters,
+                                       w.plan.splits > 1 ? (int)w.tiles : 0);
     if (e != cudaSuccess) return e;
     // x' stage counts: 192 KB of planes next to two 16 KB codes stages
     if (g.bits == 4) {

@@ -44,6 +44,7 @@
 // pairs with the packed fp32 FMA of sm_100 (__ffma2_rn). Subnormal operands
 // are handled by FMA at full rate as long as flush-to-zero is off, which is
 // the compiler default used for this library.
+#include <atomic>
 #include <cfloat>
 
 #include "common.cuh"
@@ -162,6 +163,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
     float* emax = reinterpret_cast<float*>(mbar_all + 2 * p.slots * p.ns) + (size_t)p.slots * p.ns * p.wpr * VPAD;
     uint32_t* fills = reinterpret_cast<uint32_t*>(emax + p.slots * p.wpr * NB) + slot * p.ns;
 
+    // Programmatic dependent launch: the next kernel on the stream may be
+    // scheduled now, and this one reads nothing in global memory before every
+    // earlier kernel on the stream has completed (no-ops without the launch
+    // attribute).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int total_slots = (int)gridDim.x * p.slots;
     const int gslot = (int)blockIdx.x * p.slots + slot;
     const int n_iters_total = (p.M + R - 1) / R;
@@ -477,11 +484,26 @@ cudaError_t launch_t(GemvParams p, cudaStream_t s) {
     // per stage: a consumed mbarrier and the warps' partial sums; then emax
     const size_t red_b = sizeof(float) * (size_t)p.slots * p.wpr * 8;   // one stage's partial sums
     const size_t tail = sizeof(float) * (size_t)p.slots * p.wpr * NB + sizeof(uint32_t) * (size_t)p.slots * kMaxStages;
-    // stages: as many as fit while keeping every CTA the registers allow resident
-    cudaFuncAttributes attr;
-    cudaError_t e = cudaFuncGetAttributes(&attr, kern);
+    // Host setup cached per device: the kernel's register count, the
+    // shared-memory opt-in (set once to the largest size a launch may ask for)
+    // and the occupancy of the last (threads, shared memory) pair.
+    constexpr int kDevs = 32;
+    static std::atomic<int> regs_c[kDevs], optin_c[kDevs];
+    static std::atomic<uint64_t> occ_c[kDevs];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    int occ_regs = attr.numRegs > 0 ? 65536 / (attr.numRegs * threads) : 1;
+    const bool cached = dev >= 0 && dev < kDevs;
+    int num_regs = cached ? regs_c[dev].load(std::memory_order_relaxed) : 0;
+    if (num_regs == 0) {
+        cudaFuncAttributes attr;
+        e = cudaFuncGetAttributes(&attr, kern);
+        if (e != cudaSuccess) return e;
+        num_regs = attr.numRegs > 0 ? attr.numRegs : 1;
+        if (cached) regs_c[dev].store(num_regs, std::memory_order_relaxed);
+    }
+    // stages: as many as fit while keeping every CTA the registers allow resident
+    int occ_regs = 65536 / (num_regs * threads);
     if (occ_regs < 1) occ_regs = 1;
     if (occ_regs > 4) occ_regs = 4;
     int ns = 0;
@@ -493,20 +515,41 @@ cudaError_t launch_t(GemvParams p, cudaStream_t s) {
     if (ns < 2) ns = 2;
     p.ns = ns;
     const size_t smem = (size_t)p.slots * ns * p.stage_bytes + 16 * (size_t)p.slots * ns + red_b * ns + tail;
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    constexpr int kOptIn = 220 * 1024;
+    if (smem > (size_t)kOptIn) return cudaErrorInvalidValue;
+    if (!cached || optin_c[dev].load(std::memory_order_relaxed) == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kOptIn);
+        if (e != cudaSuccess) return e;
+        if (cached) optin_c[dev].store(1, std::memory_order_relaxed);
+    }
+    const uint64_t key = ((uint64_t)smem << 16) | (uint64_t)threads;   // occupancy in the low byte
+    const uint64_t hit = cached ? occ_c[dev].load(std::memory_order_relaxed) : 0;
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
-    if (e != cudaSuccess) return e;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
+    if (hit != 0 && (hit >> 8) == key) {
+        occ = (int)(hit & 0xFF);
+    } else {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+        if (e != cudaSuccess) return e;
+        if (occ < 1) return cudaErrorInvalidConfiguration;
+        if (cached) occ_c[dev].store((key << 8) | (uint64_t)(occ & 0xFF), std::memory_order_relaxed);
+    }
     const int64_t iters = ((int64_t)p.M + R - 1) / R;
     int64_t grid = (int64_t)sm_count() * occ;
     const int64_t need = (iters + p.slots - 1) / p.slots;
     if (grid > need) grid = need;
     if (grid < 1) grid = 1;
-    kern<<<(unsigned)grid, threads, smem, s>>>(p);
-    return cudaGetLastError();
+    // launched with programmatic stream serialization (see the kernel's first lines)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr_pdl[1];
+    attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr_pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int BITS, bool LEAN>
