@@ -38,7 +38,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 M_ROWS, K_COLS, GROUP = 28672, 8192, 128
-E2E_CHUNKS = 4
+E2E_CHUNKS = 8
 WORKLOAD = "sharded_28672x8192_int4_g128"
 METRIC = "dequant-GEMM weight-stream GB/s & GFLOP/s vs B200 roofline, batch 1–4096"
 
