@@ -394,9 +394,38 @@ __global__ void __launch_bounds__(WideCfg<NT, MT>::THREADS, 1)
                 float sum[E];
 #pragma unroll
                 for (int i = 0; i < E; ++i) sum[i] = 0.0f;
-                for (int64_t c = cf; c <= cl; ++c) {
+                // Small layers give a row block dozens of contributors: the
+                // slots are loaded U at a time (U x E floats in registers,
+                // which the accumulators no longer hold) and added in CTA order.
+                constexpr int U = E <= 8 ? 8 : (E <= 16 ? 4 : 2);
+                auto slot = [&](int64_t c) {
                     const int wh = unit_start(c, p.units, P) < ub ? 1 : 0;
-                    const float* src = p.part + ((size_t)(2 * c + wh) * C::MMA_THREADS + threadIdx.x) * E;
+                    return p.part + ((size_t)(2 * c + wh) * C::MMA_THREADS + threadIdx.x) * E;
+                };
+                int64_t c = cf;
+#pragma unroll 1
+                for (; c + U - 1 <= cl; c += U) {
+                    float4 q[U][E / 4];
+#pragma unroll
+                    for (int j = 0; j < U; ++j) {
+                        const float* src = slot(c + j);
+#pragma unroll
+                        for (int i = 0; i < E / 4; ++i) q[j][i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+                    }
+#pragma unroll
+                    for (int j = 0; j < U; ++j) {
+#pragma unroll
+                        for (int i = 0; i < E / 4; ++i) {
+                            sum[4 * i] += q[j][i].x;
+                            sum[4 * i + 1] += q[j][i].y;
+                            sum[4 * i + 2] += q[j][i].z;
+                            sum[4 * i + 3] += q[j][i].w;
+                        }
+                    }
+                }
+#pragma unroll 1
+                for (; c <= cl; ++c) {
+                    const float* src = slot(c);
 #pragma unroll
                     for (int i = 0; i < E; i += 4) {
                         const float4 q = __ldcg(reinterpret_cast<const float4*>(src + i));
