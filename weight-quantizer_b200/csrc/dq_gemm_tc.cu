@@ -166,7 +166,9 @@ struct Cfg {
     static constexpr int LAUNCH_REGS = (65536 / (THREADS * MINB)) / 8 * 8;
     static constexpr int REGS_CTL = 40;
     static constexpr int REGS_DQ = BN >= 128 ? 112 : 88;
-    static constexpr int REGS_EPI = BN >= 128 ? 232 : 112;
+    // the epilogue of the 192-wide tile holds 192 accumulators and one
+    // 32-column load: it takes the 16 registers the other roles leave over
+    static constexpr int REGS_EPI = BN > 128 ? 248 : (BN >= 128 ? 232 : 112);
     // Batch tiles of 32 (batches 5-32) stack the hi and lo planes into one
     // MMA of N = 2 BN (the lo rows follow the hi rows in every K tile of the
     // planes), halving the MMA instructions, which bound this narrow tile;
@@ -696,14 +698,14 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACCW);
             if constexpr (BN > 128) {
-                // 16 columns per load: BN accumulators plus the loaded chunk
-                // stay inside the epilogue's register budget
+                // 32 columns per load (each load waits for its data: fewer,
+                // wider loads drain the accumulator in fewer round trips)
 #pragma unroll
-                for (int cc = 0; cc < BN / 16; ++cc) {
-                    float v[16];
-                    tmem_ld16(taddr + 16u * cc, v);
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    float v[32];
+                    tmem_ld32(taddr + 32u * cc, v);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) acc[cc * 16 + i] = fmaf(sc, v[i], acc[cc * 16 + i]);
+                    for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
                 }
             } else {
                 // stacked planes: the hi sums, then the lo sums BN columns further
