@@ -39,8 +39,8 @@
 // warp 1 allocates tensor memory and one thread issues tcgen05.mma (M = 128,
 // N = BN, K = 16, A from tensor memory) and tcgen05.commit, learning which
 // tiles are ready from one shared word that warp 3 publishes after waiting on
-// their barriers. Then one or two dequant warpgroups (see Cfg) and one
-// epilogue warpgroup. All hand-offs are mbarriers; every wait is bounded and,
+// their barriers. Then one or two dequant warpgroups and one or two epilogue
+// warpgroups (see Cfg). All hand-offs are mbarriers; every wait is bounded and,
 // on expiry, records bit 0 in the library's fault word and stops waiting.
 // Every TMA and bulk load targets this CTA's own shared memory only.
 //
@@ -147,18 +147,27 @@ __device__ __forceinline__ void set_regs() {
     }
 }
 
-// Launch shape per batch tile. Wide tiles (BN >= 128): two dequant
-// warpgroups (each writes one K tile of every A stage), one CTA per SM with
-// all 512 columns of tensor memory. Narrow tiles: one dequant warpgroup, two
-// CTAs per SM (half the tensor memory each) so that one CTA's hand-off
-// latency overlaps the other's work. After entering their roles the
+// Launch shape per batch tile. Wide tiles (BN >= 128): one CTA per SM with
+// all 512 columns of tensor memory and four warpgroups: N = 128 runs two
+// dequant warpgroups (each writes one K tile of every A stage) and one
+// epilogue warpgroup; N = 192 one dequant and two epilogue warpgroups (each
+// reads 96 columns of every group accumulator: with one, the accumulator
+// drain took longer than the next group's MMAs and held the MMA back).
+// Narrow tiles: one dequant and one epilogue warpgroup, two CTAs per SM (half
+// the tensor memory each) so that one CTA's hand-off latency overlaps the
+// other's work. After entering their roles the
 // warpgroups re-split the launch's registers with setmaxnreg; the split must
 // not exceed the launch's registers (checked here and, for the per-thread
 // count ptxas chose, again before the launch).
 template <int BN>
 struct Cfg {
-    static constexpr int DQG = BN >= 128 ? 2 : 1;          // dequant warpgroups
-    static constexpr int THREADS = (2 + DQG) * 128;
+    // The 192-wide tile drains its accumulators with two epilogue warpgroups
+    // (96 columns each: a group's accumulator is read in half the time) and
+    // dequantizes with one; the 128-wide tile the other way round.
+    static constexpr int EPG = BN > 128 ? 2 : 1;            // epilogue warpgroups
+    static constexpr int DQG = BN == 128 ? 2 : 1;           // dequant warpgroups
+    static constexpr int EW = BN / EPG;                     // accumulator columns per epilogue thread
+    static constexpr int THREADS = (1 + DQG + EPG) * 128;
     static constexpr int WARP_EPI0 = kWarpDq0 + 4 * DQG;
     static constexpr int DQ_WARPS = 4 * DQG;
     static constexpr int MINB = BN >= 128 ? 1 : 2;        // CTAs per SM
@@ -166,16 +175,14 @@ struct Cfg {
     static constexpr int LAUNCH_REGS = (65536 / (THREADS * MINB)) / 8 * 8;
     static constexpr int REGS_CTL = 40;
     static constexpr int REGS_DQ = BN >= 128 ? 112 : 88;
-    // the epilogue of the 192-wide tile holds 192 accumulators and one
-    // 32-column load: it takes the 16 registers the other roles leave over
-    static constexpr int REGS_EPI = BN > 128 ? 248 : (BN >= 128 ? 232 : 112);
+    static constexpr int REGS_EPI = BN > 128 ? 176 : (BN >= 128 ? 232 : 112);
     // Batch tiles of 32 (batches 5-32) stack the hi and lo planes into one
     // MMA of N = 2 BN (the lo rows follow the hi rows in every K tile of the
     // planes), halving the MMA instructions, which bound this narrow tile;
     // the accumulator then holds sum A hi and sum A lo side by side.
     static constexpr bool STACK = BN <= 32;
     static constexpr int ACCW = STACK ? 2 * BN : BN;      // tensor-memory columns per accumulator
-    static_assert(REGS_CTL + DQG * REGS_DQ + REGS_EPI <= (2 + DQG) * LAUNCH_REGS,
+    static_assert(REGS_CTL + DQG * REGS_DQ + EPG * REGS_EPI <= (1 + DQG + EPG) * LAUNCH_REGS,
                   "register split exceeds the launch's registers");
 };
 constexpr int kCodeRowBytes = 128;  // packed code bytes per row per codes stage
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
-            mbar_init(acc_empty(b), 4);   // one arrival per epilogue warp
+            mbar_init(acc_empty(b), 4 * C::EPG);   // one arrival per epilogue warp
         }
         *reinterpret_cast<volatile uint32_t*>(smem + L::READY) = 0u;
         fence_mbarrier_init();
@@ -672,14 +679,17 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
         }
     } else {
         set_regs<C::REGS_EPI, C::LAUNCH_REGS>();
-        // ---- epilogue: thread owns row r of the tile, all BN columns -----------
+        // ---- epilogue: thread owns row r of the tile, EW of the BN columns
+        // (epilogue warpgroup e: columns c0 .. c0 + EW - 1) ------------------------
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
+        constexpr int EW = C::EW;
         const int64_t m = m0 + r;
         const int64_t srow = p.scale_rows == 1 ? 0 : min(m, (int64_t)p.M - 1);
-        float acc[BN];
+        const int c0 = C::EPG == 1 ? 0 : ((warp - kWarpEpi0) >> 2) * EW;
+        float acc[EW];
 #pragma unroll
-        for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < EW; ++i) acc[i] = 0.0f;
         // scales of groups g + 1 .. g + 4 are in flight while group g is read
         const float* srow_p = p.scales + srow * p.groups + G0();
         float sc_n1 = NGL() > 1 ? __ldg(srow_p + 1) : 0.0f;
@@ -701,9 +711,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                 // 32 columns per load (each load waits for its data: fewer,
                 // wider loads drain the accumulator in fewer round trips)
 #pragma unroll
-                for (int cc = 0; cc < BN / 32; ++cc) {
+                for (int cc = 0; cc < EW / 32; ++cc) {
                     float v[32];
-                    tmem_ld32(taddr + 32u * cc, v);
+                    tmem_ld32(taddr + (uint32_t)c0 + 32u * cc, v);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) acc[cc * 32 + i] = fmaf(sc, v[i], acc[cc * 32 + i]);
                 }
@@ -728,9 +738,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             const float dz = zc - zero_int(zc);
             if (__any_sync(0xffffffffu, dz != 0.0f)) {
                 const float cz = -(sc * dz);
-                const float4* xs = reinterpret_cast<const float4*>(p.xsum + (int64_t)(G0() + g) * p.bpad + n0);
+                const float4* xs = reinterpret_cast<const float4*>(p.xsum + (int64_t)(G0() + g) * p.bpad + n0 + c0);
 #pragma unroll
-                for (int i = 0; i < BN / 4; ++i) {
+                for (int i = 0; i < EW / 4; ++i) {
                     const float4 v = __ldg(xs + i);
                     acc[4 * i] = fmaf(cz, v.x, acc[4 * i]);
                     acc[4 * i + 1] = fmaf(cz, v.y, acc[4 * i + 1]);
@@ -756,9 +766,9 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             const size_t tile_stride = (size_t)p.tiles_m * p.tiles_n * BN * BM;
             float* mine = p.part + (size_t)blockIdx.y * tile_stride + (size_t)tile * BN * BM;
 #pragma unroll
-            for (int i = 0; i < BN; ++i) mine[i * BM + r] = acc[i];
+            for (int i = 0; i < EW; ++i) mine[(c0 + i) * BM + r] = acc[i];
             __threadfence();
-            named_barrier(1, 128);   // the epilogue warpgroup
+            named_barrier(1, 128 * C::EPG);   // the epilogue warpgroups
             volatile uint32_t* flag = reinterpret_cast<volatile uint32_t*>(smem + L::FLAG);
             if (warp == kWarpEpi0 && lane == 0) {
                 const int prev = atomicAdd(p.counters + tile, 1);
@@ -766,16 +776,16 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
                 if (last) p.counters[tile] = 0;
                 *flag = last ? 1u : 0u;
             }
-            named_barrier(1, 128);
+            named_barrier(1, 128 * C::EPG);
             write = *flag != 0u;
             if (write) {
                 __threadfence();
 #pragma unroll
-                for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+                for (int i = 0; i < EW; ++i) acc[i] = 0.0f;
                 for (int sp = 0; sp < p.splits; ++sp) {
                     const float* src = p.part + (size_t)sp * tile_stride + (size_t)tile * BN * BM;
 #pragma unroll
-                    for (int i = 0; i < BN; ++i) acc[i] += __ldcg(src + i * BM + r);
+                    for (int i = 0; i < EW; ++i) acc[i] += __ldcg(src + (c0 + i) * BM + r);
                 }
             }
         }
@@ -789,21 +799,24 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, Cfg<BN>::MINB)
             // travel over NVLink while other tiles still compute. No fence:
             // the kernel's completion makes its peer stores visible to work
             // ordered after it, and the caller orders the ranks after the call.
+            // columns n0 + c0 + i, i < nv, of rows n of y: one running pointer
+            const int nv = min(EW, p.B - (n0 + c0));
+            const float* is = p.inv_s + n0 + c0;
             if (p.y_all != nullptr) {
                 // one store reaches every rank's y through the NVLink switch
+                float* yp = p.y_all + (int64_t)(n0 + c0) * p.ldy + m;
 #pragma unroll
-                for (int i = 0; i < BN; ++i) {
-                    const int n = n0 + i;
-                    if (n < p.B)
-                        st_all_ranks(p.y_all + (int64_t)n * p.ldy + m, __fadd_rn(__fmul_rn(acc[i], __ldg(p.inv_s + n)), bm));
+                for (int i = 0; i < EW; ++i) {
+                    if (i < nv) st_all_ranks(yp, __fadd_rn(__fmul_rn(acc[i], __ldg(is + i)), bm));
+                    yp += p.ldy;
                 }
             } else {
                 for (int d = 0; d <= p.n_extra; ++d) {
-                    float* dst = d == 0 ? p.y : p.y_extra[d - 1];
+                    float* yp = (d == 0 ? p.y : p.y_extra[d - 1]) + (int64_t)(n0 + c0) * p.ldy + m;
 #pragma unroll
-                    for (int i = 0; i < BN; ++i) {
-                        const int n = n0 + i;
-                        if (n < p.B) dst[(int64_t)n * p.ldy + m] = __fadd_rn(__fmul_rn(acc[i], __ldg(p.inv_s + n)), bm);
+                    for (int i = 0; i < EW; ++i) {
+                        if (i < nv) *yp = __fadd_rn(__fmul_rn(acc[i], __ldg(is + i)), bm);
+                        yp += p.ldy;
                     }
                 }
             }
