@@ -232,7 +232,10 @@ def awq_search(
         if a == 0.0:
             pre = np.ones(w.shape[1], dtype=np.float32)
         else:
-            p = (mag.astype(np.float64) ** a).astype(np.float32)
+            # torch's pow on an fp32 tensor takes the scalar exponent as fp32
+            # (0.3 becomes 0.300000012); the power of that exponent is taken
+            # in fp64 and rounded once to fp32
+            p = (mag.astype(np.float64) ** float(np.float32(a))).astype(np.float32)
             mean = np.float32(p.astype(np.float64).mean())
             mean = max(mean, np.float32(1e-8))
             pre = (p / mean).astype(np.float32)

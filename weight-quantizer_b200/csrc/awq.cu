@@ -43,7 +43,10 @@ __global__ void __launch_bounds__(kColThreads) channel_abs_sum_kernel(const floa
 }
 
 // One block: s_k = m_k^alpha, then the mean in fp64 over a fixed tree, then
-// s_k / max(mean, 1e-8) rounded to fp32.
+// s_k / max(mean, 1e-8) rounded to fp32. The power is taken in fp64 and
+// rounded once to fp32, which gives the correctly rounded fp32 power except
+// where the exact value lies within a few fp64 ulps of a rounding boundary:
+// a value defined by the mathematics, not by one math library's fp32 pow.
 constexpr int kPreThreads = 1024;
 __global__ void __launch_bounds__(kPreThreads) pre_scale_kernel(const float* __restrict__ mag, int64_t K, float alpha,
                                                                float* __restrict__ pre) {
@@ -54,7 +57,7 @@ __global__ void __launch_bounds__(kPreThreads) pre_scale_kernel(const float* __r
     }
     double s = 0.0;
     for (int64_t k = threadIdx.x; k < K; k += kPreThreads) {
-        const float p = powf(mag[k], alpha);
+        const float p = (float)pow((double)mag[k], (double)alpha);
         pre[k] = p;
         s += (double)p;
     }
