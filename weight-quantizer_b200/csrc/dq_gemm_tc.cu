@@ -44,8 +44,9 @@
 // on expiry, records bit 0 in the library's fault word and stops waiting.
 // Every TMA and bulk load targets this CTA's own shared memory only.
 //
-// Output tiles are rasterized in bands of 16 batch tiles so the x' planes of a
-// band stay resident in L2 while the weights stream about twice.
+// Output tiles are rasterized in bands of batch tiles sized so that the x'
+// planes of a band (at most 40 MB) stay resident in L2 while the weights
+// stream past once per band.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
