@@ -238,3 +238,31 @@ def test_integer_zero_points_unchanged_by_correction(wq, cuda) -> None:
     a = wq._kernels.dequant_gemm(x, qw.codes, qw.scales, qw.zeros, None, 128, 4)
     b = wq._kernels.dequant_gemm(x, qw.codes, qw.scales, (qw.zeros + 0.0).contiguous(), None, 128, 4)
     assert torch.equal(a, b)
+
+
+def test_wide_batch_tiles_vs_oracle(wq, orc, cuda) -> None:
+    """Batches of 1024 and more run the 192-wide tensor-core tile (the tiles of
+    the other tests are 32, 64 and 128 wide). Cases with enough output tiles
+    that K is not split: int4 g128 symmetric; int4 g64 asymmetric with a
+    channel scale and a ragged last batch tile; int8 with an odd number of
+    128-row weight tiles; fractional zero points. Each result is checked
+    against the oracle and repeated bit for bit."""
+    g = torch.Generator().manual_seed(1234)
+    cases = ((2048, 1024, 1024, 4, True, 128, False, False),
+             (2304, 768, 1200, 4, False, 64, True, False),
+             (1664, 2048, 1100, 8, False, 128, False, False),
+             (2048, 1024, 1056, 4, False, 128, False, True))
+    for M, K, B, bits, sym, group, pre, frac in cases:
+        qw = _rand_layer(wq, g, M, K, bits, sym, group, pre)
+        z = qw.zeros.cpu().clone()
+        if frac:
+            z[M // 2:] += torch.rand(z[M // 2:].shape, generator=g) - 0.5
+        x = torch.randn(B, K, generator=g)
+        ch = qw.channel_scale
+        got = wq._kernels.dequant_gemm(x.to(cuda), qw.codes, qw.scales, z.to(cuda), ch, qw.group_size, bits)
+        again = wq._kernels.dequant_gemm(x.to(cuda), qw.codes, qw.scales, z.to(cuda), ch, qw.group_size, bits)
+        assert torch.equal(got, again)
+        ref = orc.dequant_gemm(x.numpy(), qw.codes.cpu().numpy(), qw.scales.cpu().numpy(), z.numpy(),
+                               None if ch is None else ch.cpu().numpy(), qw.group_size, bits)
+        assert_close_y(got.cpu().numpy(), ref, f"bits{bits} {M}x{K} g{group} b{B} frac{frac}")
+        assert wq._kernels.fault_status() == 0
