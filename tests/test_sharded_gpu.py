@@ -1,8 +1,8 @@
 """Row-sharded dequant-GEMM on GPUs: the permute kernel, the one-rank layer, and
 (with two or more GPUs) the NCCL and peer-store exchanges compared with the
 unsharded layer, at batches that run each kernel's multi-output epilogue
-(1: the batch-1/2 decode kernel, 8: the batch 3-32 kernel, 64: the tcgen05
-kernel)."""
+(1: the batch-1/2 decode kernel, 8: the batch 3-32 kernel, 64 and 1024: the
+tcgen05 kernel's 64- and 192-wide tiles)."""
 
 from __future__ import annotations
 
@@ -75,7 +75,7 @@ def _nccl_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     lin = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="nccl")
     p2p = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="p2p")
     nvls = sharded.RowParallelDequantLinear(shard, M, rank, world, exchange="nvls")
-    for b in (1, 8, 64):
+    for b in (1, 8, 64, 1024):
         x = torch.randn(b, K, generator=g).to(dev)
         y = lin.forward(x)
         np.save(os.path.join(out_dir, f"y{rank}_b{b}.npy"), y.cpu().numpy())
@@ -101,7 +101,7 @@ def test_row_parallel_nccl_matches_unsharded(wq, cuda, tmp_path) -> None:
     M, K = 3001, 4096
     w = torch.randn(M, K, generator=g) * 0.02
     qw = wq.quantize_weight(w.to(cuda), wq.QuantConfig(bits=4, symmetric=True, group_size=128))
-    for b in (1, 8, 64):
+    for b in (1, 8, 64, 1024):
         x = torch.randn(b, K, generator=g).to(cuda)
         expect = wq.dequant_gemm(x, qw, impl="kernel").cpu().numpy()
         for r in range(world):
