@@ -387,7 +387,7 @@ def config_lines(wq: Any, wl: Any, dev: Any, stream: Any, peaks: dict[str, Any],
     sample_rows = 256
     gms_sample = gpu_ms(lambda: gq.gptq_quantize(wd[:sample_rows], hd, gcfg))
     gptq = {"layer": "4096x4096 int4 sym g128, Hessian of 8192 rows", "ms": round(gms, 2),
-            "timed": "factorization (cuSOLVER), qparams, sweep and tail kernels, host reads of their flags"}
+            "timed": "factorization, qparams, sweep and tail kernels (all this library's), host reads of their flags"}
     if ref_rtn is not None:
         ref_gptq = importlib.import_module("ptqkit.gptq")
         rq = ref_rtn.QuantConfig(bits=4, symmetric=True, group_size=128, method=ref_rtn.Method.GPTQ)

@@ -274,6 +274,21 @@ WQ_API int wq_gptq_tail_f64(double* w, int64_t rows, int64_t ld, int64_t c0, int
                             const double* err_block, int count, const double* hinv, int64_t ldh, int64_t s0,
                             void* stream);
 
+/* Upper Cholesky factor of the inverse of a symmetric positive definite     */
+/* matrix: U with U^T U = A^-1, the factor the sweep above reads (replaces    */
+/* the torch.linalg.cholesky, cholesky_inverse and upper cholesky calls of    */
+/* src/ptqkit/gptq.py:59-66). A fp64 [n, lda] device (only the upper triangle */
+/* is read), U fp64 [n, ldu] device (zeros below the diagonal), workspace of  */
+/* wq_chol_inverse_upper_workspace_bytes(n). info (int32 device word): the    */
+/* call sets it to 0, and to 1 + a column index when a pivot is not positive  */
+/* and finite (A not numerically positive definite; U is then not valid).     */
+/* U = J M^-1 J with M M^T = J A J (J reverses rows and columns): one blocked */
+/* factorization and one blocked triangular inverse, all on this library's    */
+/* kernels; the caller reads info after the stream completes.                 */
+WQ_API size_t wq_chol_inverse_upper_workspace_bytes(int64_t n);
+WQ_API int wq_chol_inverse_upper_f64(const double* a, int64_t n, int64_t lda, double* u, int64_t ldu,
+                                     void* workspace, size_t workspace_bytes, int32_t* info, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Row-sharded layers across the GPUs of one node. No counterpart in ptqkit, */
 /* whose kernel runs on one CPU and splits rows across OpenMP threads        */

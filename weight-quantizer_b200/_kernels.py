@@ -76,6 +76,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "wq_gptq_block_f64": (
         _int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _vp, _i64, _int, _vp, _i64, _vp, _vp, _vp, _vp]),
     "wq_gptq_tail_f64": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _int, _vp, _i64, _i64, _vp]),
+    "wq_chol_inverse_upper_workspace_bytes": (_sz, [_i64]),
+    "wq_chol_inverse_upper_f64": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "wq_dequant_gemm_f32_multi": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
@@ -636,3 +638,21 @@ def gptq_tail(w: torch.Tensor, c0: int, err_block: torch.Tensor, hinv: torch.Ten
     _check(library().wq_gptq_tail_f64(_ptr(w), rows, int(w.stride(0)), int(c0), ncols, _ptr(err_block), count,
                                       _ptr(hinv), int(hinv.stride(0)), int(s0), _stream(dev)))
 
+
+def chol_inverse_upper(a: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """U with U^T U = a^-1 (a symmetric positive definite, fp64, on the GPU;
+    its upper triangle is read): the factor of gptq.py:59-66, on this
+    library's kernels. Returns (U, info): info is a one-element int32 device
+    tensor, 0, or 1 + a column whose pivot was not positive and finite (U is
+    then not valid); nothing here waits for the GPU."""
+    dev = _cuda_device([a])
+    if a.dtype != torch.float64 or a.ndim != 2 or a.shape[0] != a.shape[1] or a.stride(1) != 1:
+        raise ValueError("a must be a square row-major fp64 matrix")
+    n = int(a.shape[0])
+    u = torch.empty((n, n), dtype=torch.float64, device=dev)
+    info = torch.empty(1, dtype=torch.int32, device=dev)
+    ws_bytes = int(library().wq_chol_inverse_upper_workspace_bytes(n))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    _check(library().wq_chol_inverse_upper_f64(_ptr(a), n, int(a.stride(0)), _ptr(u), n, _ptr(ws), ws_bytes,
+                                               _ptr(info), _stream(dev)))
+    return u, info

@@ -547,4 +547,21 @@ int wq_gptq_tail_f64(double* w, int64_t rows, int64_t ld, int64_t c0, int64_t nc
     return e == cudaSuccess ? WQ_OK : cuda_fail(e);
 }
 
+size_t wq_chol_inverse_upper_workspace_bytes(int64_t n) {
+    return n <= 0 ? 0 : wq::chol_inverse_upper_workspace_bytes(n);
+}
+
+int wq_chol_inverse_upper_f64(const double* a, int64_t n, int64_t lda, double* u, int64_t ldu, void* workspace,
+                              size_t workspace_bytes, int32_t* info, void* stream) {
+    if (n < 0) return WQ_E_NEG_DIM;
+    if (info == nullptr) return WQ_E_NULL;
+    if (n > 0 && (lda < n || ldu < n)) return WQ_E_LD;
+    if (n > 0 && (a == nullptr || u == nullptr || workspace == nullptr)) return WQ_E_NULL;
+    if (n > 0 && workspace_bytes < wq::chol_inverse_upper_workspace_bytes(n)) return WQ_E_WORKSPACE;
+    if (n > 46340) return WQ_E_TOO_LARGE;   // n * n elements indexed by the rotation's grid
+    cudaError_t e = wq::launch_chol_inverse_upper(a, n, lda, u, ldu, static_cast<double*>(workspace), info,
+                                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? WQ_OK : cuda_fail(e);
+}
+
 }  // extern "C"

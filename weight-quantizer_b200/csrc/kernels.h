@@ -123,6 +123,10 @@ cudaError_t launch_gptq_block(const double* w, int64_t rows, int64_t ld, const d
                               int64_t s0, int count, const double* scale, const double* zero, int64_t qp_stride,
                               int bits, int32_t* codes, int64_t ldc, double* err_block, const uint8_t* zero_err,
                               int* bad_col, cudaStream_t s);
+// upper Cholesky factor of an inverse (chol.cu)
+size_t chol_inverse_upper_workspace_bytes(int64_t n);
+cudaError_t launch_chol_inverse_upper(const double* a, int64_t n, int64_t lda, double* u, int64_t ldu,
+                                      double* work, int* info, cudaStream_t s);
 cudaError_t launch_gptq_tail(double* work, int64_t rows, int64_t ld, int64_t c0, int64_t ncols, const double* err,
                              int count, const double* hinv, int64_t ldh, int64_t s0, cudaStream_t s);
 

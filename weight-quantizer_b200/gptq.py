@@ -12,18 +12,22 @@ percdamp * mean(diag) to the diagonal, retry with a larger bump if the
 factorization fails). Group scales come from the updated weights at the start
 of each group, per-channel and per-tensor scales once before the sweep.
 
-Device split: the factorization is cuSOLVER through torch.linalg (a plain
-library factorization, once per layer); the sweep runs in this library's
-kernels (``wq_gptq_qparams_f64``: the grid of quant.py:146-172 in fp64;
-``wq_gptq_block_f64``: one block's column sweep, one warp per weight row,
-bit-exact with ptqkit's _obs_block given the same inputs;
-``wq_gptq_tail_f64``: each block's update of the later columns, the
+Device split: everything runs in this library's kernels. The factor U
+(``wq_chol_inverse_upper_f64``) is computed as J M^-1 J with M M^T = J H J
+(J reverses rows and columns), one blocked factorization and one blocked
+triangular inverse, where the reference factors H, inverts it and factors the
+inverse (the same matrix, rounded differently); a pivot that is not positive
+retries with more damping as the reference does. The sweep:
+``wq_gptq_qparams_f64`` (the grid of quant.py:146-172 in fp64),
+``wq_gptq_block_f64`` (one block's column sweep, one warp per weight row,
+bit-exact with ptqkit's _obs_block given the same inputs) and
+``wq_gptq_tail_f64`` (each block's update of the later columns, the
 O(K^2 M) part, an fp64 tile kernel summing in column order). Groups wider
 than 128 columns are swept in 128-column blocks whose later columns are
 corrected by that update, the same updates as the reference's per-column
 ones in a different summation order.
 
-Because the factorization and the GEMMs round differently from the CPU
+Because the factorization and the tail update round differently from the CPU
 LAPACK/BLAS the reference runs on, codes agree with ptqkit's except where a
 weight lands within rounding of a grid edge; the tests bound that fraction
 and the output error.
@@ -57,12 +61,9 @@ def _factor_inverse(hessian: torch.Tensor, percdamp: float) -> torch.Tensor:
     h = h.clone()
     h[eye, eye] = h[eye, eye] + damp
     for _ in range(6):
-        chol, info = torch.linalg.cholesky_ex(h)
+        factor, info = _kernels.chol_inverse_upper(h)
         if int(info.item()) == 0:
-            inv = torch.cholesky_inverse(chol)
-            factor, info2 = torch.linalg.cholesky_ex(inv, upper=True)
-            if int(info2.item()) == 0:
-                return factor
+            return factor
         bump = torch.mean(torch.diag(h)) * 0.1 + 1e-6
         h[eye, eye] = h[eye, eye] + bump
     raise RuntimeError("damped Hessian Cholesky failed")
