@@ -83,12 +83,12 @@ def test_gptq_entry_point_validation(wq) -> None:
     assert lib.wq_gptq_tail_f64(d, 2, 8, 4, 8, d, 4, d, 16, 0, None) == 20
     assert lib.wq_gptq_tail_f64(None, 2, 16, 4, 8, d, 4, d, 16, 0, None) == 11
     # the factor of the inverse: sizes, strides, pointers, workspace (no GPU work)
-    assert lib.wq_chol_inverse_upper_workspace_bytes(100) == 100 * 100 * 8
+    assert lib.wq_chol_inverse_upper_workspace_bytes(100) == 2 * 100 * 100 * 8
     assert lib.wq_chol_inverse_upper_workspace_bytes(0) == 0
     assert lib.wq_chol_inverse_upper_f64(d, -1, 4, d, 4, d, 1 << 20, d, None) == 5
     assert lib.wq_chol_inverse_upper_f64(d, 4, 4, d, 4, d, 1 << 20, None, None) == 11
     assert lib.wq_chol_inverse_upper_f64(d, 8, 4, d, 8, d, 1 << 20, d, None) == 20
     assert lib.wq_chol_inverse_upper_f64(d, 8, 8, d, 7, d, 1 << 20, d, None) == 20
     assert lib.wq_chol_inverse_upper_f64(None, 8, 8, d, 8, d, 1 << 20, d, None) == 11
-    assert lib.wq_chol_inverse_upper_f64(d, 8, 8, d, 8, d, 8 * 8 * 8 - 1, d, None) == 12
+    assert lib.wq_chol_inverse_upper_f64(d, 8, 8, d, 8, d, 2 * 8 * 8 * 8 - 1, d, None) == 12
     assert lib.wq_chol_inverse_upper_f64(d, 50000, 50000, d, 50000, d, 1 << 62, d, None) == 13

@@ -13,9 +13,11 @@
 //      diagonal block factored in shared memory by one CTA, the panel below it
 //      by forward substitution (one thread per row), the trailing lower
 //      triangle updated with 64 x 64 tiles (4 x 4 per thread);
-//   2. X = M^-1, blocked from the bottom-right block up: the diagonal block
-//      inverted in shared memory, the panel below it as
-//      X21 = -(X22 M21) X11 with X22 already inverted;
+//   2. X = M^-1 by doubling: every 64 x 64 diagonal block inverted in shared
+//      memory (one launch), then levels of S = 1, 2, 4, ... blocks: each pair
+//      of neighbouring inverted diagonal sections A (upper) and C (lower) of
+//      S blocks gets its off-diagonal part X_CA = -X_C (M_CA X_A), two batched
+//      64 x 64-tile products per level over all pairs at once;
 //   3. U = J X J (a 180-degree rotation of the matrix, in place), zero below
 //      the diagonal.
 //
@@ -56,10 +58,10 @@ __global__ void __launch_bounds__(256) potrf_diag_kernel(double* __restrict__ l,
         if (tid == 0) s[k][k] = d;
         for (int i = k + 1 + tid; i < b; i += 256) s[i][k] = s[i][k] / d;
         __syncthreads();
-        const int m = b - k - 1;
-        for (int idx = tid; idx < m * m; idx += 256) {
-            const int r = k + 1 + idx / m, c = k + 1 + idx % m;
-            if (c <= r) s[r][c] = s[r][c] - s[r][k] * s[c][k];
+        // trailing triangle of the block: a 16 x 16 grid of threads over (r, c)
+        for (int r = k + 1 + (tid >> 4); r < b; r += 16) {
+            const double lrk = s[r][k];
+            for (int c = k + 1 + (tid & 15); c <= r; c += 16) s[r][c] = s[r][c] - lrk * s[c][k];
         }
         __syncthreads();
     }
@@ -69,8 +71,9 @@ __global__ void __launch_bounds__(256) potrf_diag_kernel(double* __restrict__ l,
     }
 }
 
-// Panel below the diagonal block: rows i >= j0 + b solve x L11^T = a, one
-// warp of 32 rows per CTA, one row per lane, the row in shared memory.
+// Panel below the diagonal block: rows i >= j0 + b solve x L11^T = a by
+// forward substitution, one warp of 32 rows per CTA, one row per lane, the
+// row in shared memory.
 constexpr int kTrsmRows = 32;
 __global__ void __launch_bounds__(kTrsmRows) trsm_panel_kernel(double* __restrict__ l, int64_t n, int64_t j0, int b) {
     __shared__ double ld[kNB][kNB];          // the factored diagonal block
@@ -84,10 +87,12 @@ __global__ void __launch_bounds__(kTrsmRows) trsm_panel_kernel(double* __restric
     const bool valid = i < n;
     for (int k = 0; k < b; ++k) xs[k][lane] = valid ? l[i * n + j0 + k] : 0.0;
     __syncthreads();
+    // column-oriented: once x_k is final, it updates every later x_q (those
+    // updates are independent of one another)
     for (int k = 0; k < b; ++k) {
-        double v = xs[k][lane];
-        for (int q = 0; q < k; ++q) v = v - xs[q][lane] * ld[k][q];
-        xs[k][lane] = v / ld[k][k];
+        const double xk = xs[k][lane] / ld[k][k];
+        xs[k][lane] = xk;
+        for (int q = k + 1; q < b; ++q) xs[q][lane] = xs[q][lane] - xk * ld[q][k];
     }
     if (valid)
         for (int k = 0; k < b; ++k) l[i * n + j0 + k] = xs[k][lane];
@@ -148,9 +153,11 @@ __global__ void __launch_bounds__(256) syrk_kernel(double* __restrict__ l, int64
 // memory: element (i, j), j <= i, at i (i + 1) / 2 + j.
 __device__ __forceinline__ int tri(int i, int j) { return i * (i + 1) / 2 + j; }
 __global__ void __launch_bounds__(kNB) trtri_diag_kernel(const double* __restrict__ l, int64_t n,
-                                                         double* __restrict__ x, int64_t ldx, int64_t j0, int b) {
+                                                         double* __restrict__ x, int64_t ldx) {
     __shared__ double lp[kNB * (kNB + 1) / 2];
     __shared__ double xp[kNB * (kNB + 1) / 2];
+    const int64_t j0 = (int64_t)blockIdx.x * kNB;
+    const int b = (int)min((int64_t)kNB, n - j0);
     const int c = threadIdx.x;
     for (int idx = c; idx < b * b; idx += kNB) {
         const int r = idx / b, q = idx % b;
@@ -171,33 +178,44 @@ __global__ void __launch_bounds__(kNB) trtri_diag_kernel(const double* __restric
     }
 }
 
-// Panel of the inverse: rows i >= s = j0 + b, columns [j0, j0 + b):
-// X[i, :] = -(sum_{s <= k <= i} X[i, k] L[k, :]) X11, one 64-row tile of
-// rows per CTA (4 x 4 outputs per thread). Dynamic shared memory: the two
-// staging tiles of the first product, then Y and X11 for the second.
-constexpr size_t kTrmmSmem = (size_t)(kT * (kT + 1) + kNB * kNB) * sizeof(double);
-__global__ void __launch_bounds__(256) trmm_panel_kernel(const double* __restrict__ l, int64_t n,
-                                                         double* __restrict__ x, int64_t ldx, int64_t j0, int b) {
-    extern __shared__ double smem_d[];
-    double (*es)[kT + 1] = reinterpret_cast<double (*)[kT + 1]>(smem_d);                 // [k][row]
-    double (*hs)[kT] = reinterpret_cast<double (*)[kT]>(smem_d + kKc * (kT + 1));        // [k][col]
-    const int64_t s = j0 + b, m = n - s;
-    const int64_t rt0 = (int64_t)blockIdx.x * kT;   // first row of the tile, relative to s
+// One doubling level of the inverse. Pair g: A = rows/columns [a0, c0), C =
+// rows/columns [c0, c1) with a0 = 2 g S 64, c0 = a0 + S 64. Phase 1:
+// T[i, j] = sum_k M[i, k] X[k, j] (i in C, j, k in A, k >= j's tile); phase 2:
+// X[i, j] = -sum_k X[i, k] T[k, j] (i, k in C, k up to i's tile). X's
+// diagonal 64-blocks hold zeros above their diagonals, and no product reads
+// a block of X above the block diagonal. 64 x 64 output tiles (4 x 4 per
+// thread), the k sum in order in chunks of 16.
+template <bool PHASE2>
+__global__ void __launch_bounds__(256) inv_level_kernel(const double* __restrict__ mm, double* __restrict__ x,
+                                                        int64_t ldx, double* __restrict__ t, int64_t n, int64_t S) {
+    const int64_t a0 = (int64_t)blockIdx.y * 2 * S * kT, c0 = a0 + S * kT;
+    if (c0 >= n) return;
+    const int64_t c1 = min(c0 + S * kT, n);
+    const int64_t ti = (int64_t)blockIdx.x / S, tj = (int64_t)blockIdx.x % S;
+    const int64_t i0 = c0 + ti * kT, j0 = a0 + tj * kT;
+    if (i0 >= c1) return;
+    __shared__ double es[kKc][kT + 1];   // [k][row]
+    __shared__ double hs[kKc][kT];       // [k][col]
+    const double* aop = PHASE2 ? x : mm;
+    const int64_t lda = PHASE2 ? ldx : n;
+    const double* bop = PHASE2 ? t : x;
+    const int64_t ldb = PHASE2 ? n : ldx;
+    const int64_t klo = PHASE2 ? c0 : j0;
+    const int64_t khi = PHASE2 ? min(i0 + kT, c1) : c0;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     double acc[4][4];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[a][q] = 0.0;
-    const int64_t kend = min(m, rt0 + kT);   // X[i, k] = 0 for k > i
-    for (int64_t k0 = 0; k0 < kend; k0 += kKc) {
+    for (int64_t k0 = klo; k0 < khi; k0 += kKc) {
         for (int idx = threadIdx.x; idx < kKc * kT; idx += 256) {
             const int kk = idx % kKc, rr = idx / kKc;
-            const int64_t ri = rt0 + rr, k = k0 + kk;
-            es[kk][rr] = (ri < m && k <= ri) ? x[(s + ri) * ldx + s + k] : 0.0;
+            const int64_t i = i0 + rr, k = k0 + kk;
+            es[kk][rr] = (i < c1 && k < khi) ? aop[i * lda + k] : 0.0;
             const int cc = idx % kT, k2 = idx / kT;
-            const int64_t kb = k0 + k2;
-            hs[k2][cc] = (kb < m && cc < b) ? l[(s + kb) * n + j0 + cc] : 0.0;
+            const int64_t j = j0 + cc, kb = k0 + k2;
+            hs[k2][cc] = (j < c0 && kb < khi) ? bop[kb * ldb + j] : 0.0;
         }
         __syncthreads();
 #pragma unroll
@@ -214,41 +232,16 @@ __global__ void __launch_bounds__(256) trmm_panel_kernel(const double* __restric
         }
         __syncthreads();
     }
-    // second product: out = -Y X11 (X11 lower, from this step's diagonal inverse)
-    double (*ys)[kT + 1] = reinterpret_cast<double (*)[kT + 1]>(smem_d);
-    double (*x11)[kNB] = reinterpret_cast<double (*)[kNB]>(smem_d + kT * (kT + 1));
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) ys[ty * 4 + a][tx * 4 + q] = acc[a][q];
-    for (int idx = threadIdx.x; idx < kNB * kNB; idx += 256) {
-        const int r = idx / kNB, q = idx % kNB;
-        x11[r][q] = (r < b && q <= r) ? x[(j0 + r) * ldx + j0 + q] : 0.0;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[a][q] = 0.0;
-    for (int p = 0; p < b; ++p) {
-        double yv[4], xv[4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) yv[a] = ys[ty * 4 + a][p];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) xv[q] = x11[p][tx * 4 + q];
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[a][q] = fma(yv[a], xv[q], acc[a][q]);
-    }
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
-        const int64_t ri = rt0 + ty * 4 + a;
-        if (ri >= m) continue;
+        const int64_t i = i0 + ty * 4 + a;
+        if (i >= c1) continue;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const int cc = tx * 4 + q;
-            if (cc < b) x[(s + ri) * ldx + j0 + cc] = -acc[a][q];
+            const int64_t j = j0 + tx * 4 + q;
+            if (j >= c0) continue;
+            if constexpr (PHASE2) x[i * ldx + j] = -acc[a][q];
+            else t[i * n + j] = acc[a][q];
         }
     }
 }
@@ -268,7 +261,8 @@ __global__ void __launch_bounds__(256) rotate_upper_kernel(double* __restrict__ 
 
 }  // namespace
 
-size_t chol_inverse_upper_workspace_bytes(int64_t n) { return (size_t)n * (size_t)n * sizeof(double); }
+// workspace: M (n x n), then the doubling levels' products T (n x n)
+size_t chol_inverse_upper_workspace_bytes(int64_t n) { return 2 * (size_t)n * (size_t)n * sizeof(double); }
 
 cudaError_t launch_chol_inverse_upper(const double* a, int64_t n, int64_t lda, double* u, int64_t ldu,
                                       double* work, int* info, cudaStream_t s) {
@@ -290,15 +284,15 @@ cudaError_t launch_chol_inverse_upper(const double* a, int64_t n, int64_t lda, d
         }
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    // 2. X = M^-1 into u, from the last block up
-    e = cudaFuncSetAttribute(trmm_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTrmmSmem);
-    if (e != cudaSuccess) return e;
-    for (int64_t j0 = ((n - 1) / kNB) * kNB; j0 >= 0; j0 -= kNB) {
-        const int b = (int)min((int64_t)kNB, n - j0);
-        trtri_diag_kernel<<<1, kNB, 0, s>>>(l, n, u, ldu, j0, b);
-        const int64_t m = n - j0 - b;
-        if (m > 0)
-            trmm_panel_kernel<<<(unsigned)((m + kT - 1) / kT), 256, kTrmmSmem, s>>>(l, n, u, ldu, j0, b);
+    // 2. X = M^-1 into u: diagonal blocks, then doubling levels
+    const int64_t nb = (n + kNB - 1) / kNB;
+    trtri_diag_kernel<<<(unsigned)nb, kNB, 0, s>>>(l, n, u, ldu);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    double* t = work + n * n;
+    for (int64_t S = 1; S < nb; S *= 2) {
+        const dim3 grid((unsigned)(S * S), (unsigned)((nb + 2 * S - 1) / (2 * S)));
+        inv_level_kernel<false><<<grid, 256, 0, s>>>(l, u, ldu, t, n, S);
+        inv_level_kernel<true><<<grid, 256, 0, s>>>(l, u, ldu, t, n, S);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     // 3. U = J X J, upper
