@@ -517,8 +517,9 @@ def ours(args: argparse.Namespace) -> None:
     kernel_flops = 2.0 * B * mp * K_COLS
     achieved_tflops = kernel_flops / t_kernel / 1e12
     # DRAM bytes (read + write) of one tensor-core launch at batch 4096 on one
-    # GPU, from the ncu capture summarised in profiles/dq_gemm_tc_28672x8192_b4096.md
-    traffic = 0.842342e9 + 0.459466e9 if (B == 4096 and world == 1) else None
+    # GPU, from the latest ncu capture of this kernel summarised in
+    # profiles/dq_gemm_tc_28672x8192_b4096.md (memory-side counters)
+    traffic = 0.746892e9 + 0.454140e9 if (B == 4096 and world == 1) else None
     roofline = {"bound": "tensor", "achieved": round(achieved_tflops, 3), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
                 "traffic_unit": "bytes per launch",
