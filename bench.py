@@ -559,10 +559,10 @@ def ours(args: argparse.Namespace) -> None:
         kt2 = []
         for _ in range(args.steps):
             flush_l2(len(kt2))
-            # ~0.1 ms of device-side wait: the host has enqueued the call before
+            # ~0.5 ms of device-side wait: the host has enqueued the call before
             # the device reaches e0, so the host's launch latency stays outside
             # the kernel's time
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(1_000_000)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             lin.forward_local(xb, out=local_out[:b])
